@@ -1,0 +1,137 @@
+/*
+ * nsq.h -- C ABI of libnsq, the B200 (sm_100a) quantized-linear library.
+ *
+ * Each entry point replaces one operation of nanoSGLang's quantized-linear
+ * path (xiehuanyi/nanoSGLang, nano_sglang/decode/quantization.py) and takes
+ * the reference's own buffer layouts, unchanged:
+ *   AWQ: qweight int32 [N, K/8] (nibble i of word j = column 8j+i),
+ *        scales fp16 [N, G], zeros fp16 [N, G], G = ceil(K / group_size).
+ *   FP8: weight_fp8 e4m3 [N, K] row-major, weight_scale one fp32 (device).
+ * x is row-major [M, K], y is row-major [M, N], both in the activation dtype.
+ *
+ * Conventions
+ *   - All pointers are device pointers; `stream` is a cudaStream_t (may be 0).
+ *   - Every call is stream-ordered and asynchronous; nothing allocates or
+ *     frees device memory, nothing synchronises the host, so every call can
+ *     be captured in a CUDA graph. Workspaces belong to the caller.
+ *   - Shapes, dtypes and alignment are validated on the host before any
+ *     launch; a violation returns an error code and launches nothing.
+ *   - Kernels never trap: a bounded on-device wait that runs out records
+ *     NSQ_EDEVICE_TIMEOUT in the library's device status word, readable with
+ *     nsq_device_status().
+ */
+#ifndef NSQ_H_
+#define NSQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of activations / bias */
+#define NSQ_DTYPE_NONE (-1)
+#define NSQ_DTYPE_F16 0
+#define NSQ_DTYPE_BF16 1
+#define NSQ_DTYPE_F32 2
+
+/* return codes */
+#define NSQ_OK 0
+#define NSQ_EINVAL 1          /* bad shape, size or argument */
+#define NSQ_EALIGN 2          /* pointer or stride not aligned as required */
+#define NSQ_ENOTSUP 3         /* device is not sm_100 / shape not supported */
+#define NSQ_ECUDA 4           /* CUDA runtime/driver error at launch */
+#define NSQ_EWORKSPACE 5      /* workspace missing or too small */
+#define NSQ_EDEVICE_TIMEOUT 6 /* a bounded device-side wait ran out */
+
+/* Human-readable text for a return code (static storage). */
+const char* nsq_strerror(int code);
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+int nsq_version(void);
+
+/* Device status word: 0 when no kernel has reported a problem since the last
+ * reset, else an NSQ_E* code. `where`/`block` (may be NULL) receive the tag
+ * of the wait that gave up and the block index. Synchronises the device. */
+int nsq_device_status(int* where, int* block);
+int nsq_device_status_reset(void);
+
+/*
+ * AWQ unpack + dequantise, bit-exact:
+ *   w_out[n, k] = fp16( fp16(q[n,k] - zeros[n, k/gs]) * scales[n, k/gs] )
+ * Replaces AWQLinear._dequantize (quantization.py:126-148).
+ * Requires K % 8 == 0 (the reference raises otherwise), group_size >= 1,
+ * qweight/w_out 16-byte aligned.
+ */
+int nsq_awq_dequant(const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
+                    uint16_t* w_out, int64_t N, int64_t K, int64_t group_size, void* stream);
+
+/*
+ * AWQ W4A16 linear:  y = x @ dequant(qweight, scales, zeros)^T + bias.
+ * Replaces AWQLinear.forward (quantization.py:150-152). x_dtype is F16 or
+ * BF16 (y has the same dtype; the reference accepts fp16 only and raises on
+ * bf16). bias_dtype is NONE/F16/BF16/F32. Requires K % 32 == 0,
+ * group_size % 128 == 0, x/y/qweight 16-byte aligned.
+ * M <= 64 runs the split-K tensor-core GEMV (workspace unused); larger M runs
+ * the tcgen05 GEMM. Workspace may be NULL (none is needed by either).
+ */
+int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
+                   const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
+                   int64_t group_size, const void* bias, int bias_dtype, void* y,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * FP8 W8A16 linear:  y = x @ (float(weight_fp8) * weight_scale)^T + bias.
+ * Replaces FP8Linear.forward (quantization.py:49-52). weight_scale points to
+ * ONE fp32 on the device (the reference's 0-dim / [1] buffer) and is read on
+ * the device, never on the host. Requires K % 16 == 0, x/y/weight 16-byte
+ * aligned. Workspace may be NULL.
+ */
+int nsq_fp8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
+                   const uint8_t* weight_fp8, const float* weight_scale, const void* bias,
+                   int bias_dtype, void* y, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/*
+ * FP8 dequantise, bit-exact with the reference's weight materialisation
+ * `weight_fp8.to(dtype) * weight_scale` (quantization.py:51):
+ *   w_out[n, k] = round_to_out_dtype(float(e4m3) * weight_scale).
+ * out_dtype is F16 or BF16.
+ */
+int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* w_out,
+                    int out_dtype, int64_t N, int64_t K, void* stream);
+
+/*
+ * AWQ quantiser, bit-exact with AWQLinear.from_linear
+ * (quantization.py:154-194): per (row, group) asymmetric min/max int4,
+ * sequential nibble packing, columns past 8*(K/8) dropped. w is row-major
+ * [N, K] in w_dtype (F16/BF16/F32). Writes qweight [N, K/8], scales/zeros
+ * [N, G] fp16. Requires K >= 8.
+ */
+int nsq_awq_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int64_t group_size,
+                     int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream);
+
+/* Bytes of device workspace nsq_fp8_quantize needs (absmax reduction). */
+size_t nsq_fp8_quantize_workspace_size(int64_t N, int64_t K);
+
+/*
+ * FP8 quantiser, bit-exact with FP8Linear.from_linear (quantization.py:54-75):
+ * scale = absmax / 448 (1 if absmax == 0), codes = RNE e4m3 of w / scale,
+ * non-saturating like torch's cast. Writes weight_fp8 [N, K] and the scale
+ * (one fp32, device). workspace >= nsq_fp8_quantize_workspace_size().
+ */
+int nsq_fp8_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* weight_fp8,
+                     float* weight_scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Opt in (1) or out (0, default) of programmatic dependent launch for the
+ * linear kernels: with it on, a linear starts streaming its weights while the
+ * previous kernel on the stream drains. Only valid when no kernel earlier on
+ * the stream writes the weights being read. Returns the previous setting. */
+int nsq_set_pdl(int enable);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSQ_H_ */

@@ -1,0 +1,282 @@
+// C ABI of libnsq (declared in include/nsq.h): host-side validation, device
+// capability checks, tensor-map encoding and dispatch to the kernels.
+//
+// Validation happens before any launch and mirrors the reference's own
+// failure modes where it has them (e.g. in_features % 8 != 0 raises in
+// AWQLinear._dequantize, quantization.py:134-137); everything else the
+// kernels need (alignment, K multiples for TMA) is reported as an error code.
+#include <mutex>
+#include <atomic>
+
+#include "nsq_common.cuh"
+#include "nsq_internal.h"
+
+namespace nsq {
+
+__device__ DevStatus g_device_status;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+int g_sms[kMaxDevices] = {0};
+int g_arch_ok[kMaxDevices] = {0};  // 0 unknown, 1 ok, -1 not sm_100
+DevStatus* g_status_ptr[kMaxDevices] = {nullptr};
+std::atomic<int> g_pdl{0};
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return (d >= 0 && d < kMaxDevices) ? d : -1;
+}
+
+// NSQ_OK if the current device is an sm_100 part, else an error code.
+int check_device() {
+  const int d = current_device();
+  if (d < 0) return NSQ_ECUDA;
+  if (g_arch_ok[d] == 1) return NSQ_OK;
+  if (g_arch_ok[d] == -1) return NSQ_ENOTSUP;
+  std::lock_guard<std::mutex> lk(g_mu);
+  int major = 0, minor = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, d) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess) {
+    return NSQ_ECUDA;
+  }
+  g_sms[d] = sms;
+  g_arch_ok[d] = (major == 10 && minor == 0) ? 1 : -1;
+  return g_arch_ok[d] == 1 ? NSQ_OK : NSQ_ENOTSUP;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline bool valid_act_dtype(int t) { return t == NSQ_DTYPE_F16 || t == NSQ_DTYPE_BF16; }
+inline bool valid_bias_dtype(int t) {
+  return t == NSQ_DTYPE_NONE || t == NSQ_DTYPE_F16 || t == NSQ_DTYPE_BF16 || t == NSQ_DTYPE_F32;
+}
+
+constexpr int64_t kIntMax = 0x7FFFFFFF;
+
+}  // namespace
+
+int num_sms() {
+  const int d = current_device();
+  if (d < 0) return 148;
+  if (g_sms[d] == 0) check_device();
+  return g_sms[d] > 0 ? g_sms[d] : 148;
+}
+
+DevStatus* device_status_ptr() {
+  const int d = current_device();
+  if (d < 0) return nullptr;
+  if (g_status_ptr[d] != nullptr) return g_status_ptr[d];
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_status_ptr[d] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    g_status_ptr[d] = static_cast<DevStatus*>(p);
+  }
+  return g_status_ptr[d];
+}
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
+CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
+                              uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                              uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  if (g_encode == nullptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_encode == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                           &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr) {
+        return CUDA_ERROR_NOT_FOUND;
+      }
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return g_encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace nsq
+
+using namespace nsq;
+
+extern "C" {
+
+const char* nsq_strerror(int code) {
+  switch (code) {
+    case NSQ_OK: return "ok";
+    case NSQ_EINVAL: return "invalid argument (shape, size or dtype)";
+    case NSQ_EALIGN: return "pointer or row stride not 16-byte aligned";
+    case NSQ_ENOTSUP: return "unsupported device (needs sm_100) or unsupported shape";
+    case NSQ_ECUDA: return "CUDA error while launching";
+    case NSQ_EWORKSPACE: return "workspace missing or too small";
+    case NSQ_EDEVICE_TIMEOUT: return "a bounded device-side wait ran out (kernel wound down)";
+    default: return "unknown nsq error";
+  }
+}
+
+int nsq_version(void) { return 100; }
+
+int nsq_set_pdl(int enable) { return g_pdl.exchange(enable ? 1 : 0); }
+
+int nsq_device_status(int* where, int* block) {
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  DevStatus st{};
+  if (cudaMemcpyFromSymbol(&st, g_device_status, sizeof(st)) != cudaSuccess) return NSQ_ECUDA;
+  if (where) *where = static_cast<int>(st.where);
+  if (block) *block = static_cast<int>(st.block);
+  return static_cast<int>(st.code);
+}
+
+int nsq_device_status_reset(void) {
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  DevStatus st{};
+  return cudaMemcpyToSymbol(g_device_status, &st, sizeof(st)) == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+int nsq_awq_dequant(const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
+                    uint16_t* w_out, int64_t N, int64_t K, int64_t group_size, void* stream) {
+  if (N < 0 || K <= 0 || group_size <= 0 || K % 8 != 0) return NSQ_EINVAL;
+  if (N == 0) return NSQ_OK;
+  if (!qweight || !scales || !zeros || !w_out) return NSQ_EINVAL;
+  if (!aligned16(qweight) || !aligned16(w_out) || ((K * 2) % 16) != 0) return NSQ_EALIGN;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  cudaError_t e = launch_awq_dequant(qweight, scales, zeros, w_out, N, K, group_size,
+                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* w_out,
+                    int out_dtype, int64_t N, int64_t K, void* stream) {
+  if (N < 0 || K <= 0 || !valid_act_dtype(out_dtype)) return NSQ_EINVAL;
+  if (N == 0) return NSQ_OK;
+  if (!weight_fp8 || !weight_scale || !w_out) return NSQ_EINVAL;
+  if (!aligned16(weight_fp8) || !aligned16(w_out)) return NSQ_EALIGN;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  cudaError_t e = launch_fp8_dequant(weight_fp8, weight_scale, w_out, out_dtype, N * K,
+                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+static int linear_common(LinearArgs& a, cudaStream_t stream) {
+  if (a.M == 0) return NSQ_OK;
+  if (a.M <= kDecodeMaxM) return run_decode_linear(a, stream);
+  return run_prefill_linear(a, stream);
+}
+
+int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
+                   const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
+                   int64_t group_size, const void* bias, int bias_dtype, void* y,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (M < 0 || K <= 0 || N <= 0 || M > kIntMax || K > kIntMax || N > kIntMax) return NSQ_EINVAL;
+  if (!valid_act_dtype(x_dtype) || !valid_bias_dtype(bias_dtype)) return NSQ_EINVAL;
+  if ((bias_dtype == NSQ_DTYPE_NONE) != (bias == nullptr)) return NSQ_EINVAL;
+  if (group_size <= 0 || group_size % 128 != 0) return NSQ_ENOTSUP;
+  if (K % 32 != 0) return NSQ_ENOTSUP;  // qweight rows must be a 16-byte multiple for TMA
+  if (M == 0) return NSQ_OK;
+  if (!x || !qweight || !scales || !zeros || !y) return NSQ_EINVAL;
+  if (!aligned16(x) || !aligned16(y) || !aligned16(qweight)) return NSQ_EALIGN;
+  if (M <= kDecodeMaxM && K > 8 * 64 * 128) return NSQ_ENOTSUP;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  LinearArgs a{};
+  a.fmt = 0;
+  a.x = x;
+  a.x_bf16 = x_dtype == NSQ_DTYPE_BF16;
+  a.M = (int)M;
+  a.K = (int)K;
+  a.N = (int)N;
+  a.wq = qweight;
+  a.scales = scales;
+  a.zeros = zeros;
+  a.group_size = (int)group_size;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.y = y;
+  return linear_common(a, static_cast<cudaStream_t>(stream));
+}
+
+int nsq_fp8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
+                   const uint8_t* weight_fp8, const float* weight_scale, const void* bias,
+                   int bias_dtype, void* y, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  if (M < 0 || K <= 0 || N <= 0 || M > kIntMax || K > kIntMax || N > kIntMax) return NSQ_EINVAL;
+  if (!valid_act_dtype(x_dtype) || !valid_bias_dtype(bias_dtype)) return NSQ_EINVAL;
+  if ((bias_dtype == NSQ_DTYPE_NONE) != (bias == nullptr)) return NSQ_EINVAL;
+  if (K % 16 != 0) return NSQ_ENOTSUP;  // weight rows must be a 16-byte multiple for TMA
+  if (M == 0) return NSQ_OK;
+  if (!x || !weight_fp8 || !weight_scale || !y) return NSQ_EINVAL;
+  if (!aligned16(x) || !aligned16(y) || !aligned16(weight_fp8)) return NSQ_EALIGN;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  LinearArgs a{};
+  a.fmt = 1;
+  a.x = x;
+  a.x_bf16 = x_dtype == NSQ_DTYPE_BF16;
+  a.M = (int)M;
+  a.K = (int)K;
+  a.N = (int)N;
+  a.wq = weight_fp8;
+  a.wscale = weight_scale;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.y = y;
+  return linear_common(a, static_cast<cudaStream_t>(stream));
+}
+
+int nsq_awq_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int64_t group_size,
+                     int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream) {
+  if (N < 0 || K < 8 || group_size <= 0) return NSQ_EINVAL;
+  if (!(w_dtype == NSQ_DTYPE_F16 || w_dtype == NSQ_DTYPE_BF16 || w_dtype == NSQ_DTYPE_F32)) {
+    return NSQ_EINVAL;
+  }
+  if (N == 0) return NSQ_OK;
+  if (!w || !qweight || !scales || !zeros) return NSQ_EINVAL;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  cudaError_t e = launch_awq_quantize(w, w_dtype, N, K, group_size, qweight, scales, zeros,
+                                      static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+size_t nsq_fp8_quantize_workspace_size(int64_t N, int64_t K) {
+  (void)N;
+  (void)K;
+  return 256;
+}
+
+int nsq_fp8_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* weight_fp8,
+                     float* weight_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  if (N < 0 || K < 0) return NSQ_EINVAL;
+  if (!(w_dtype == NSQ_DTYPE_F16 || w_dtype == NSQ_DTYPE_BF16 || w_dtype == NSQ_DTYPE_F32)) {
+    return NSQ_EINVAL;
+  }
+  if (!weight_scale || (N * K > 0 && (!w || !weight_fp8))) return NSQ_EINVAL;
+  if (!workspace || workspace_bytes < nsq_fp8_quantize_workspace_size(N, K)) return NSQ_EWORKSPACE;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  cudaError_t e = launch_fp8_quantize(w, w_dtype, N * K, weight_fp8, weight_scale, workspace,
+                                      static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,55 @@
+// Host-side declarations shared by libnsq's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nsq {
+
+struct DevStatus;
+
+int num_sms();                  // SM count of the current device (cached per device)
+DevStatus* device_status_ptr(); // device address of this device's status word (lazily set up)
+bool pdl_enabled();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (libnsq does
+// not link libcuda directly, so it also loads on machines without a driver).
+CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
+                              uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                              uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+
+// elementwise
+cudaError_t launch_awq_dequant(const int32_t* qweight, const uint16_t* scales,
+                               const uint16_t* zeros, uint16_t* out, int64_t N, int64_t K,
+                               int64_t gs, cudaStream_t stream);
+cudaError_t launch_fp8_dequant(const uint8_t* w, const float* scale, void* out, int out_dtype,
+                               int64_t total, cudaStream_t stream);
+cudaError_t launch_awq_quantize(const void* w, int dtype, int64_t N, int64_t K, int64_t gs,
+                                int32_t* qweight, uint16_t* scales, uint16_t* zeros,
+                                cudaStream_t stream);
+cudaError_t launch_fp8_quantize(const void* w, int dtype, int64_t total, uint8_t* codes,
+                                float* scale, void* workspace, cudaStream_t stream);
+
+// linears. fmt: 0 = AWQ int4, 1 = FP8 e4m3. Return an NSQ_* code.
+struct LinearArgs {
+  int fmt;
+  const void* x;
+  int x_bf16;
+  int M, K, N;
+  const void* wq;          // qweight (AWQ) or weight_fp8 (FP8)
+  const uint16_t* scales;  // AWQ
+  const uint16_t* zeros;   // AWQ
+  int group_size;          // AWQ
+  const float* wscale;     // FP8
+  const void* bias;
+  int bias_dtype;
+  void* y;
+};
+int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64
+int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M
+
+constexpr int kDecodeMaxM = 64;
+
+}  // namespace nsq

@@ -1,0 +1,471 @@
+// Prefill-regime quantized linear (any M; used for M > 64): a dense
+// contraction on the 5th-generation tensor cores.
+//
+// Replaces AWQLinear.forward / FP8Linear.forward (nano_sglang/decode/
+// quantization.py:150-152, :49-52), whose reference path materialises the
+// whole dequantised weight in HBM and then calls cuBLAS.
+//
+// Persistent, warp-specialised kernel, one 128-token x 256-feature output
+// tile at a time per CTA, fp32 accumulators in tensor memory:
+//   warp 0        TMA producer: x tile [128 x 64] (128-byte swizzle) and the
+//                 packed weight tile [256 rows x 64 columns] of the reference
+//                 layout into a 4-stage ring.
+//   warp 1        tcgen05.mma issuer (one thread), 128x256x16 kind::f16 steps;
+//                 also owns the 512-column TMEM allocation (2 accumulators).
+//   warps 2..9    converters: one weight row per thread; unpack int4 (AWQ,
+//                 zero point and group scale applied) or e4m3 (FP8) into the
+//                 MMA element type, written in the UMMA 128-byte-swizzled
+//                 K-major layout into a 2-stage ring.
+//   warps 10..13  epilogue: tcgen05.ld of the finished accumulator, per-tensor
+//                 scale (FP8), bias, rounding to the activation dtype, store.
+// The accumulator is double-buffered so the epilogue of tile i overlaps the
+// main loop of tile i+1. Every mbarrier wait is bounded.
+#include <atomic>
+
+#include "nsq_common.cuh"
+#include "nsq_internal.h"
+
+namespace nsq {
+
+namespace {
+
+constexpr int BM = 128;  // tokens per tile (UMMA M, TMEM lanes)
+constexpr int BN = 256;  // output features per tile (UMMA N, TMEM columns)
+constexpr int BK = 64;   // columns per k-block (one 128-byte swizzle row of 16-bit)
+constexpr int NL = 4;    // load stages
+constexpr int NB = 2;    // converted-weight stages
+constexpr int kWarpTma = 0;
+constexpr int kWarpMma = 1;
+constexpr int kWarpConv0 = 2;
+constexpr int kConvWarps = 8;
+constexpr int kWarpEpi0 = kWarpConv0 + kConvWarps;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+constexpr uint32_t kTmemCols = 2 * BN;
+constexpr int kXTileBytes = BM * BK * 2;  // 16 KB
+constexpr int kBTileBytes = BN * BK * 2;  // 32 KB
+
+template <int FMT>
+struct PreFmt;
+template <>
+struct PreFmt<0> {  // AWQ: 256 rows x 8 words (32 B per row), 32-byte swizzle
+  static constexpr int kWcBytes = BN * BK / 2;
+  static constexpr int kRowBytes = 32;
+};
+template <>
+struct PreFmt<1> {  // FP8: 256 rows x 64 B, 64-byte swizzle
+  static constexpr int kWcBytes = BN * BK;
+  static constexpr int kRowBytes = 64;
+};
+
+struct PrefillParams {
+  const __half* scales;
+  const __half* zeros;
+  const float* wscale;
+  const void* bias;
+  void* y;
+  DevStatus* status;
+  int M, K, N;
+  int group_size, G;
+  int bias_dtype;
+  int num_m_tiles, num_n_tiles, num_kb;
+};
+
+template <int FMT>
+struct Smem {
+  static constexpr int kX = 0;
+  static constexpr int kB = kX + NL * kXTileBytes;
+  static constexpr int kWc = kB + NB * kBTileBytes;
+  static constexpr int kBar = kWc + NL * PreFmt<FMT>::kWcBytes;
+  // barriers: full_l[NL], empty_l[NL], full_b[NB], empty_b[NB], full_acc[2], empty_acc[2]
+  static constexpr int kNumBars = 2 * NL + 2 * NB + 4;
+  static constexpr int kTmemSlot = kBar + kNumBars * 8;
+  static constexpr int kAbort = kTmemSlot + 4;
+  static constexpr int kTotal = kAbort + 4;
+  static constexpr int kAlloc = kTotal + 1024;  // room to align the base to 1 KB
+};
+
+// Per-row dequant parameters for one AWQ group, in the MMA element type.
+template <bool BF16>
+struct AwqRowParams {
+  uint32_t s2;      // {s, s}
+  uint32_t zb2;     // {magic + z, magic + z}      (exact path)
+  uint32_t magic2;  // {magic, magic}              (general path)
+  uint32_t c2;      // {-z*s, -z*s}                (general path)
+  bool exact;
+};
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float v) {
+  if constexpr (BF16) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(v, v);
+    return *reinterpret_cast<uint32_t*>(&b);
+  } else {
+    __half2 h = __floats2half2_rn(v, v);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ AwqRowParams<BF16> awq_row_params(float s, float z) {
+  AwqRowParams<BF16> r;
+  constexpr float kMagic = Magic<BF16>::kValue;
+  constexpr float kZMax = BF16 ? 127.0f : 1023.0f;
+  r.exact = (z == rintf(z)) && fabsf(z) <= kZMax;
+  if constexpr (BF16) {
+    r.s2 = pack2<true>(s);
+  } else {
+    r.s2 = pack2<false>(s);  // s is an fp16 value: exact
+  }
+  r.zb2 = pack2<BF16>(kMagic + z);
+  r.magic2 = pack2<BF16>(kMagic);
+  r.c2 = pack2<BF16>(-z * s);
+  return r;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t dq2(uint32_t e, const AwqRowParams<BF16>& rp) {
+  if constexpr (BF16) {
+    const __nv_bfloat162 ev = *reinterpret_cast<const __nv_bfloat162*>(&e);
+    const __nv_bfloat162 s = *reinterpret_cast<const __nv_bfloat162*>(&rp.s2);
+    __nv_bfloat162 o;
+    if (rp.exact) {
+      o = __hmul2(__hsub2(ev, *reinterpret_cast<const __nv_bfloat162*>(&rp.zb2)), s);
+    } else {
+      o = __hfma2(__hsub2(ev, *reinterpret_cast<const __nv_bfloat162*>(&rp.magic2)), s,
+                  *reinterpret_cast<const __nv_bfloat162*>(&rp.c2));
+    }
+    return *reinterpret_cast<uint32_t*>(&o);
+  } else {
+    const __half2 ev = *reinterpret_cast<const __half2*>(&e);
+    const __half2 s = *reinterpret_cast<const __half2*>(&rp.s2);
+    __half2 o;
+    if (rp.exact) {
+      o = __hmul2(__hsub2(ev, *reinterpret_cast<const __half2*>(&rp.zb2)), s);
+    } else {
+      o = __hfma2(__hsub2(ev, *reinterpret_cast<const __half2*>(&rp.magic2)), s,
+                  *reinterpret_cast<const __half2*>(&rp.c2));
+    }
+    return *reinterpret_cast<uint32_t*>(&o);
+  }
+}
+
+template <int FMT, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
+    const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+    const PrefillParams p) {
+  using L = Smem<FMT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* full_l = bars;
+  uint64_t* empty_l = bars + NL;
+  uint64_t* full_b = bars + 2 * NL;
+  uint64_t* empty_b = bars + 2 * NL + NB;
+  uint64_t* full_acc = bars + 2 * NL + 2 * NB;
+  uint64_t* empty_acc = full_acc + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int i = 0; i < NL; ++i) {
+      mbar_init(&full_l[i], 1);
+      mbar_init(&empty_l[i], kConvWarps + 1);
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&full_b[i], kConvWarps);
+      mbar_init(&empty_b[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full_acc[i], 1);
+      mbar_init(&empty_acc[i], kEpiWarps);
+    }
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // everything below may read what the previous kernel on the stream wrote
+  pdl_wait_prior_grids();
+
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  bool ok = true;
+
+  if (warp == kWarpTma) {
+    if (lane == 0) {
+      tma_prefetch_desc(&xmap);
+      tma_prefetch_desc(&wmap);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mt = tile / p.num_n_tiles;
+        const int nt = tile - mt * p.num_n_tiles;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int s = it % NL;
+          const uint32_t r = it / NL;
+          if (!(ok = mbar_wait(&empty_l[s], (r & 1) ^ 1, p.status, 10, abort_flag))) break;
+          mbar_arrive_expect_tx(&full_l[s], kXTileBytes + PreFmt<FMT>::kWcBytes);
+          tma_load_2d(smem + L::kX + s * kXTileBytes, &xmap, &full_l[s], kb * BK, mt * BM);
+          tma_load_2d(smem + L::kWc + s * PreFmt<FMT>::kWcBytes, &wmap, &full_l[s],
+                      FMT == 0 ? kb * (BK / 8) : kb * BK, nt * BN);
+        }
+      }
+      // let in-flight copies land before the CTA can exit
+      if (!ok) {
+        const int last = it;
+        for (int j = (last > NL ? last - NL : 0); j < last; ++j) {
+          mbar_wait(&full_l[j % NL], (j / NL) & 1, nullptr, 0, nullptr);
+        }
+      }
+    }
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(BF16, BM, BN);
+      int it_l = 0, it_b = 0, tcount = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t ar = tcount >> 1;
+        if (!(ok = mbar_wait(&empty_acc[acc], (ar & 1) ^ 1, p.status, 20, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it_l, ++it_b) {
+          const int sl = it_l % NL, sb = it_b % NB;
+          if (!(ok = mbar_wait(&full_l[sl], (it_l / NL) & 1, p.status, 21, abort_flag))) break;
+          if (!(ok = mbar_wait(&full_b[sb], (it_b / NB) & 1, p.status, 22, abort_flag))) break;
+          tc_fence_after();
+          const uint64_t adesc = sw128_kmajor_desc(smem_u32(smem + L::kX + sl * kXTileBytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kB + sb * kBTileBytes));
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // +32 bytes along K inside the swizzled row = +2 in the address field
+            umma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty_l[sl]);
+          tc_commit(&empty_b[sb]);
+        }
+        if (!ok) break;
+        tc_commit(&full_acc[acc]);
+      }
+    }
+  } else if (warp < kWarpEpi0) {
+    // ---------------- converters: one weight row per thread ----------------
+    const int row = (warp - kWarpConv0) * 32 + lane;  // 0..255
+    int it_l = 0, it_b = 0;
+    int cached_group = -1, cached_n = -1;
+    AwqRowParams<BF16> rp{};
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int nt = tile % p.num_n_tiles;
+      const int n = nt * BN + row;
+      for (int kb = 0; kb < p.num_kb; ++kb, ++it_l, ++it_b) {
+        const int sl = it_l % NL, sb = it_b % NB;
+        if constexpr (FMT == 0) {
+          const int grp = (kb * BK) / p.group_size;
+          if (grp != cached_group || n != cached_n) {
+            float s = 0.f, z = 0.f;
+            if (n < p.N) {
+              s = __half2float(p.scales[(int64_t)n * p.G + grp]);
+              z = __half2float(p.zeros[(int64_t)n * p.G + grp]);
+            }
+            rp = awq_row_params<BF16>(s, z);
+            cached_group = grp;
+            cached_n = n;
+          }
+        }
+        if (!(ok = mbar_wait(&full_l[sl], (it_l / NL) & 1, p.status, 30, abort_flag))) break;
+        if (!(ok = mbar_wait(&empty_b[sb], ((it_b / NB) & 1) ^ 1, p.status, 31, abort_flag))) break;
+        const uint32_t wc = smem_u32(smem + L::kWc + sl * PreFmt<FMT>::kWcBytes) +
+                            row * PreFmt<FMT>::kRowBytes;
+        const uint32_t brow = smem_u32(smem + L::kB + sb * kBTileBytes) + row * 128;
+        if constexpr (FMT == 0) {
+          // 32-byte swizzle: 16-byte chunk c of row r sits at c ^ ((r >> 2) & 1)
+          const uint32_t sw = (row >> 2) & 1;
+          const uint4 v0 = lds128(wc + ((0 ^ sw) << 4));
+          const uint4 v1 = lds128(wc + ((1 ^ sw) << 4));
+          const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            uint32_t e[4];
+            unpack_nibble_pairs<BF16>(words[w], e);
+            // e[t] = {q_t, q_{t+4}}  ->  in-order pairs {q0,q1},{q2,q3},{q4,q5},{q6,q7}
+            const uint32_t o0 = dq2<BF16>(prmt(e[0], e[1], 0x5410), rp);
+            const uint32_t o1 = dq2<BF16>(prmt(e[2], e[3], 0x5410), rp);
+            const uint32_t o2 = dq2<BF16>(prmt(e[0], e[1], 0x7632), rp);
+            const uint32_t o3 = dq2<BF16>(prmt(e[2], e[3], 0x7632), rp);
+            sts128(brow + ((w ^ (row & 7)) << 4), o0, o1, o2, o3);
+          }
+        } else {
+          // 64-byte swizzle: 16-byte chunk c of row r sits at c ^ ((r >> 1) & 3)
+          const uint32_t sw = (row >> 1) & 3;
+#pragma unroll
+          for (int cch = 0; cch < 4; ++cch) {
+            const uint4 v = lds128(wc + ((cch ^ sw) << 4));
+            const uint32_t o0 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.x & 0xFFFFu));
+            const uint32_t o1 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.x >> 16));
+            const uint32_t o2 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.y & 0xFFFFu));
+            const uint32_t o3 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.y >> 16));
+            sts128(brow + (((2 * cch) ^ (row & 7)) << 4), o0, o1, o2, o3);
+            const uint32_t o4 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.z & 0xFFFFu));
+            const uint32_t o5 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.z >> 16));
+            const uint32_t o6 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.w & 0xFFFFu));
+            const uint32_t o7 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.w >> 16));
+            sts128(brow + (((2 * cch + 1) ^ (row & 7)) << 4), o4, o5, o6, o7);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&full_b[sb]);
+          mbar_arrive(&empty_l[sl]);
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM -> registers -> y ----------------
+    const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
+    uint16_t* y = static_cast<uint16_t*>(p.y);
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tcount) {
+      const int mt = tile / p.num_n_tiles;
+      const int nt = tile - mt * p.num_n_tiles;
+      const int acc = tcount & 1;
+      const uint32_t ar = tcount >> 1;
+      if (!(ok = mbar_wait(&full_acc[acc], ar & 1, p.status, 40, abort_flag))) break;
+      tc_fence_after();
+      const int m = mt * BM + sub * 32 + lane;
+      const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + cc * 32, r);
+        tmem_ld_wait();
+        const int nb = nt * BN + cc * 32;
+        float bl = 0.f;
+        if (p.bias_dtype != NSQ_DTYPE_NONE && nb + lane < p.N) bl = load_bias(p.bias, p.bias_dtype, nb + lane);
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float b0 = __shfl_sync(0xffffffffu, bl, 2 * i);
+          const float b1 = __shfl_sync(0xffffffffu, bl, 2 * i + 1);
+          const float v0 = fmaf(__uint_as_float(r[2 * i]), wscale, b0);
+          const float v1 = fmaf(__uint_as_float(r[2 * i + 1]), wscale, b1);
+          o[i] = (uint32_t)float_to_elem<BF16>(v0) | ((uint32_t)float_to_elem<BF16>(v1) << 16);
+        }
+        if (m < p.M) {
+          uint16_t* dst = y + (int64_t)m * p.N + nb;
+          if ((p.N & 7) == 0 && nb + 32 <= p.N) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              *reinterpret_cast<uint4*>(dst + 8 * v) =
+                  make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (nb + i < p.N) dst[i] = static_cast<uint16_t>(o[i >> 1] >> (16 * (i & 1)));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_acc[acc]);
+    }
+  }
+
+  pdl_launch_dependents();
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <int FMT, bool BF16>
+cudaError_t launch_t(const CUtensorMap& xmap, const CUtensorMap& wmap, const PrefillParams& p,
+                     int grid, cudaStream_t stream) {
+  using L = Smem<FMT>;
+  auto kern = prefill_linear_kernel<FMT, BF16>;
+  static std::atomic<bool> configured{false};
+  if (!configured.load()) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured.store(true);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  int na = 0;
+  if (pdl_enabled()) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, xmap, wmap, p);
+}
+
+}  // namespace
+
+int run_prefill_linear(const LinearArgs& a, cudaStream_t stream) {
+  CUtensorMap xmap, wmap;
+  CUresult cr = encode_tensor_map_2d(
+      &xmap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+      const_cast<void*>(a.x), (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, BK, BM,
+      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  if (a.fmt == 0) {
+    cr = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<void*>(a.wq),
+                              (uint64_t)a.K / 8, (uint64_t)a.N, (uint64_t)a.K / 2, BK / 8, BN,
+                              CU_TENSOR_MAP_SWIZZLE_32B);
+  } else {
+    cr = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<void*>(a.wq),
+                              (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, BK, BN,
+                              CU_TENSOR_MAP_SWIZZLE_64B);
+  }
+  if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  PrefillParams p{};
+  p.scales = reinterpret_cast<const __half*>(a.scales);
+  p.zeros = reinterpret_cast<const __half*>(a.zeros);
+  p.wscale = a.wscale;
+  p.bias = a.bias;
+  p.y = a.y;
+  p.status = device_status_ptr();
+  p.M = a.M;
+  p.K = a.K;
+  p.N = a.N;
+  p.group_size = a.group_size;
+  p.G = a.fmt == 0 ? (a.K + a.group_size - 1) / a.group_size : 0;
+  p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
+  p.num_m_tiles = (a.M + BM - 1) / BM;
+  p.num_n_tiles = (a.N + BN - 1) / BN;
+  p.num_kb = (a.K + BK - 1) / BK;
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int sms = num_sms();
+  const int grid = tiles < sms ? tiles : sms;
+  cudaError_t e;
+  if (a.fmt == 0) {
+    e = a.x_bf16 ? launch_t<0, true>(xmap, wmap, p, grid, stream)
+                 : launch_t<0, false>(xmap, wmap, p, grid, stream);
+  } else {
+    e = a.x_bf16 ? launch_t<1, true>(xmap, wmap, p, grid, stream)
+                 : launch_t<1, false>(xmap, wmap, p, grid, stream);
+  }
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+}  // namespace nsq

@@ -1,0 +1,352 @@
+"""Parity of the CUDA path (through the C ABI) against the CPU oracle and the
+reference-generated golden vectors. Tolerances: bit-exact for unpack,
+dequantisation and quantisation; relative Frobenius error <= 1e-2 for the
+GEMMs, against an fp32 ground truth."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from conftest import GOLDEN
+from oracle import nsq_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GEMM_TOL = 1e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from nanosglang_b200 import _lib
+    _lib.device_status_reset()
+    yield
+    code, where, block = _lib.device_status()
+    assert code == 0, f"device status {code} (wait tag {where}, block {block})"
+
+
+def _f16(u):
+    return np.asarray(u, dtype=np.uint16).view(np.float16)
+
+
+def _g(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def _to_np(t):
+    if t.dtype == torch.bfloat16:
+        return O.from_bf16_bits(t.view(torch.int16).cpu().numpy().view(np.uint16))
+    return t.float().cpu().numpy()
+
+
+def rand_awq(n, k, gs, seed, zero_mode="int", device="cuda"):
+    rng = np.random.default_rng(seed)
+    g = (k + gs - 1) // gs
+    qw = rng.integers(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=np.int64).astype(np.int32)
+    s = (rng.random((n, g)) * 0.009 + 0.001).astype(np.float16)
+    if zero_mode == "int":
+        z = rng.integers(0, 16, (n, g)).astype(np.float16)
+    elif zero_mode == "wide":
+        z = rng.integers(-300, 300, (n, g)).astype(np.float16)
+    else:
+        z = (rng.standard_normal((n, g)) * 6 + 7).astype(np.float16)
+    return (qw, s, z), tuple(torch.from_numpy(a).to(device) for a in (qw, s, z))
+
+
+def rand_x(m, k, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(m, k, generator=g).to(dtype)
+
+
+# ---------------------------------------------------------------------------
+# AWQ dequant: bit-exact
+# ---------------------------------------------------------------------------
+
+
+def test_awq_dequant_golden_bit_exact():
+    from nanosglang_b200 import ops
+    d = _g("awq_dequant_forward.npz")
+    for ci in range(int(d["ncases"][0])):
+        n, k, gs = (int(v) for v in d[f"c{ci}_meta"])
+        qw = torch.from_numpy(d[f"c{ci}_qweight"]).cuda()
+        s = torch.from_numpy(_f16(d[f"c{ci}_scales"])).cuda()
+        z = torch.from_numpy(_f16(d[f"c{ci}_zeros"])).cuda()
+        w = ops.awq_dequant(qw, s, z, k, gs)
+        assert np.array_equal(w.view(torch.int16).cpu().numpy().view(np.uint16), d[f"c{ci}_dequant"]), ci
+
+
+@pytest.mark.parametrize("n,k,gs,zm", [(9728, 896, 128, "int"), (896, 4864, 128, "frac"), (130, 1024, 256, "wide")])
+def test_awq_dequant_bit_exact_full_size(n, k, gs, zm):
+    from nanosglang_b200 import ops
+    (qw, s, z), (tq, ts, tz) = rand_awq(n, k, gs, seed=n + k, zero_mode=zm)
+    w = ops.awq_dequant(tq, ts, tz, k, gs)
+    ref = O.awq_dequant(qw, s, z, k, gs)
+    assert np.array_equal(w.view(torch.int16).cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+# ---------------------------------------------------------------------------
+# FP8 dequant / quantisers: bit-exact
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fp8_dequant_bit_exact(dtype):
+    from nanosglang_b200 import ops
+    rng = np.random.default_rng(1)
+    codes = rng.integers(0, 256, (333, 208), dtype=np.int64).astype(np.uint8)
+    codes[codes == 0x7F] = 0x7E  # skip NaN codes
+    codes[codes == 0xFF] = 0xFE
+    scale = np.float32(0.000321)
+    w = ops.fp8_dequant(torch.from_numpy(codes).cuda().view(torch.float8_e4m3fn),
+                        torch.tensor(scale).cuda(), dtype)
+    ref = O.fp8_dequant(codes, scale, "bf16" if dtype == torch.bfloat16 else "fp16")
+    assert np.array_equal(_to_np(w), ref)
+
+
+def test_awq_quantize_golden_bit_exact():
+    from nanosglang_b200 import ops
+    d = _g("awq_from_linear.npz")
+    for ci in range(int(d["ncases"][0])):
+        n, k, gs = (int(v) for v in d[f"c{ci}_meta"])
+        qw, s, z = ops.awq_quantize(torch.from_numpy(d[f"c{ci}_w"]).cuda(), gs)
+        assert np.array_equal(qw.cpu().numpy(), d[f"c{ci}_qweight"]), ci
+        assert np.array_equal(s.cpu().numpy().view(np.uint16), d[f"c{ci}_scales"]), ci
+        assert np.array_equal(z.cpu().numpy().view(np.uint16), d[f"c{ci}_zeros"]), ci
+
+
+def test_awq_quantize_large_vs_oracle():
+    from nanosglang_b200 import ops
+    rng = np.random.default_rng(7)
+    w = (rng.standard_normal((512, 4864)) * 0.02).astype(np.float32)
+    qw, s, z = ops.awq_quantize(torch.from_numpy(w).cuda(), 128)
+    rq, rs, rz = O.awq_quantize(w, 128)
+    assert np.array_equal(qw.cpu().numpy(), rq)
+    assert np.array_equal(s.cpu().numpy(), rs) and np.array_equal(z.cpu().numpy(), rz)
+
+
+def test_fp8_quantize_golden_bit_exact():
+    from nanosglang_b200.quantization import FP8Linear
+    d = _g("fp8_from_linear_forward.npz")
+    for ci in range(int(d["ncases"][0])):
+        n, k = (int(v) for v in d[f"c{ci}_meta"])
+        lin = nn.Linear(k, n, bias=False).cuda()
+        with torch.no_grad():
+            lin.weight.copy_(torch.from_numpy(d[f"c{ci}_w"]))
+        m = FP8Linear.from_linear(lin)
+        assert np.array_equal(m.weight_fp8.view(torch.uint8).cpu().numpy(), d[f"c{ci}_codes"]), ci
+        assert m.weight_scale.float().cpu().reshape(-1).numpy()[0] == d[f"c{ci}_scale"][0], ci
+        shape = list(d[f"c{ci}_scale_shape"])
+        assert list(m.weight_scale.shape) == ([] if shape == [-1] else shape), ci
+
+
+def test_fp8_quantize_special_values():
+    from nanosglang_b200 import ops
+    d = _g("scalar_casts.npz")
+    v = d["e4m3_in"][np.isfinite(d["e4m3_in"])].astype(np.float32)
+    v = v[np.abs(v) <= 448.0]
+    w = np.concatenate([v, np.array([448.0], dtype=np.float32)])  # absmax 448 -> scale exactly 1
+    w = np.resize(w, (w.size // 16) * 16).reshape(-1, 16)
+    codes, scale, _ = ops.fp8_quantize(torch.from_numpy(w).cuda())
+    rc, rs = O.fp8_quantize(w)
+    assert float(scale) == float(rs)
+    assert np.array_equal(codes.view(torch.uint8).cpu().numpy(), rc)
+
+
+# ---------------------------------------------------------------------------
+# AWQ linear (decode M <= 64 and prefill M > 64)
+# ---------------------------------------------------------------------------
+
+
+def _awq_case(m, n, k, gs, dtype, bias, zm, seed):
+    from nanosglang_b200 import ops
+    (qw, s, z), (tq, ts, tz) = rand_awq(n, k, gs, seed=seed, zero_mode=zm)
+    x = rand_x(m, k, dtype, seed + 1)
+    b = torch.randn(n, generator=torch.Generator().manual_seed(seed + 2)).to(dtype) if bias else None
+    y = ops.awq_linear(x.cuda(), tq, ts, tz, gs, None if b is None else b.cuda())
+    assert y.dtype == dtype and y.shape == (m, n)
+    ref = O.awq_linear(_to_np(x), qw, s, z, k, gs, None if b is None else _to_np(b))
+    return O.rel_fro(_to_np(y), ref)
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 16, 17, 33, 64])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_awq_linear_decode_config0_shape(m, dtype):
+    err = _awq_case(m, 9728, 896, 128, dtype, bias=False, zm="int", seed=m)
+    assert err <= GEMM_TOL, err
+
+
+@pytest.mark.parametrize("n,k,gs,zm,bias", [
+    (128, 896, 128, "int", True), (896, 4864, 128, "frac", False), (200, 512, 256, "wide", True),
+    (1000, 14336, 128, "int", False), (64, 96, 128, "int", True), (8, 65536, 128, "int", False)])
+@pytest.mark.parametrize("m", [1, 16, 64])
+def test_awq_linear_decode_shapes(n, k, gs, zm, bias, m):
+    err = _awq_case(m, n, k, gs, torch.bfloat16, bias, zm, seed=n + k + m)
+    assert err <= GEMM_TOL, err
+
+
+@pytest.mark.parametrize("m", [65, 128, 200, 1024])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_awq_linear_prefill(m, dtype):
+    err = _awq_case(m, 4864, 896, 128, dtype, bias=(m == 200), zm="int", seed=100 + m)
+    assert err <= GEMM_TOL, err
+
+
+@pytest.mark.parametrize("n,k,gs,zm", [(896, 4864, 128, "frac"), (300, 640, 256, "wide"), (128, 96, 128, "int")])
+def test_awq_linear_prefill_shapes(n, k, gs, zm):
+    err = _awq_case(333, n, k, gs, torch.bfloat16, bias=True, zm=zm, seed=n + k)
+    assert err <= GEMM_TOL, err
+
+
+def test_awq_linear_fp16_matches_reference_forward_golden():
+    """The reference's own fp16 forward outputs (cases the kernels support)."""
+    from nanosglang_b200 import ops
+    d = _g("awq_dequant_forward.npz")
+    for ci in range(int(d["ncases"][0])):
+        n, k, gs = (int(v) for v in d[f"c{ci}_meta"])
+        if gs % 128 or k % 32:
+            continue
+        x = torch.from_numpy(_f16(d[f"c{ci}_x"])).cuda()
+        b = torch.from_numpy(_f16(d[f"c{ci}_bias"])).cuda() if f"c{ci}_bias" in d else None
+        y = ops.awq_linear(x, torch.from_numpy(d[f"c{ci}_qweight"]).cuda(),
+                           torch.from_numpy(_f16(d[f"c{ci}_scales"])).cuda(),
+                           torch.from_numpy(_f16(d[f"c{ci}_zeros"])).cuda(), gs, b)
+        ref = _f16(d[f"c{ci}_y"]).astype(np.float32)
+        assert O.rel_fro(y.float().cpu().numpy(), ref) <= GEMM_TOL, ci
+
+
+def test_awq_linear_unsupported_group_size_raises():
+    from nanosglang_b200 import _lib, ops
+    (_, _, _), (tq, ts, tz) = rand_awq(64, 256, 64, seed=3)
+    with pytest.raises(_lib.NsqError):
+        ops.awq_linear(torch.randn(4, 256, device="cuda", dtype=torch.bfloat16), tq, ts, tz, 64)
+
+
+# ---------------------------------------------------------------------------
+# FP8 linear
+# ---------------------------------------------------------------------------
+
+
+def _fp8_case(m, n, k, dtype, bias, seed):
+    from nanosglang_b200 import ops
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    codes, scale = O.fp8_quantize(w)
+    x = rand_x(m, k, dtype, seed + 1)
+    b = torch.randn(n, generator=torch.Generator().manual_seed(seed + 2)).to(dtype) if bias else None
+    y = ops.fp8_linear(x.cuda(), torch.from_numpy(codes).cuda().view(torch.float8_e4m3fn),
+                       torch.tensor(scale).cuda(), None if b is None else b.cuda())
+    assert y.dtype == dtype and y.shape == (m, n)
+    ref = O.fp8_linear(_to_np(x), codes, scale, None if b is None else _to_np(b))
+    return O.rel_fro(_to_np(y), ref)
+
+
+QWEN05_SHAPES = [(896, 896), (896, 128), (896, 4864), (4864, 896)]  # (K, N)
+
+
+@pytest.mark.parametrize("kn", QWEN05_SHAPES)
+@pytest.mark.parametrize("m", [1, 8, 32, 64, 128, 1024])
+def test_fp8_linear_config1(kn, m):
+    k, n = kn
+    err = _fp8_case(m, n, k, torch.bfloat16, bias=(n == 128), seed=m * 7 + n)
+    assert err <= GEMM_TOL, err
+
+
+@pytest.mark.parametrize("m", [5, 64, 300])
+def test_fp8_linear_fp16_and_odd_shapes(m):
+    assert _fp8_case(m, 200, 112, torch.float16, bias=True, seed=m) <= GEMM_TOL
+    assert _fp8_case(m, 520, 608, torch.bfloat16, bias=False, seed=m + 1) <= GEMM_TOL
+
+
+def test_fp8_linear_vs_reference_forward_golden():
+    from nanosglang_b200 import ops
+    d = _g("fp8_from_linear_forward.npz")
+    for ci in range(int(d["ncases"][0])):
+        n, k = (int(v) for v in d[f"c{ci}_meta"])
+        if int(d[f"c{ci}_raises"][0]) or k % 16:
+            continue
+        x = torch.from_numpy(d[f"c{ci}_x"].view(np.int16)).cuda().view(torch.bfloat16)
+        b = torch.from_numpy(d[f"c{ci}_bias"].view(np.int16)).cuda().view(torch.bfloat16) \
+            if f"c{ci}_bias" in d else None
+        y = ops.fp8_linear(x, torch.from_numpy(d[f"c{ci}_codes"]).cuda().view(torch.float8_e4m3fn),
+                           torch.from_numpy(d[f"c{ci}_scale"]).cuda(), b)
+        assert O.rel_fro(_to_np(y), O.from_bf16_bits(d[f"c{ci}_y"])) <= GEMM_TOL, ci
+
+
+def test_fp8_linear_full_size_property_m8192():
+    """Config-1 largest case, checked against an fp32 torch reference built from
+    the bit-exact dequantised weight (size-independent property check)."""
+    from nanosglang_b200 import ops
+    torch.manual_seed(0)
+    w = (torch.randn(4864, 896, device="cuda") * 0.02)
+    codes, scale, _ = ops.fp8_quantize(w)
+    x = torch.randn(8192, 896, device="cuda").to(torch.bfloat16)
+    y = ops.fp8_linear(x, codes, scale)
+    wd = ops.fp8_dequant(codes, torch.ones((), device="cuda"), torch.float16).float() * scale
+    ref = x.float() @ wd.T
+    err = ((y.float() - ref).norm() / ref.norm()).item()
+    assert err <= GEMM_TOL, err
+
+
+# ---------------------------------------------------------------------------
+# Module level: drop-in classes, CUDA graphs
+# ---------------------------------------------------------------------------
+
+
+def test_modules_from_linear_forward():
+    from nanosglang_b200.quantization import AWQLinear, FP8Linear
+    torch.manual_seed(0)
+    lin = nn.Linear(896, 1152, bias=True).cuda().to(torch.bfloat16)
+    x = torch.randn(4, 7, 896, device="cuda", dtype=torch.bfloat16)
+    a = AWQLinear.from_linear(lin, 128)
+    assert a.qweight.is_cuda and a.qweight.shape == (1152, 112)
+    wdq = a._dequantize()
+    ref = x.float() @ wdq.float().T + lin.bias.float()
+    ya = a(x)
+    assert ya.shape == (4, 7, 1152) and ya.dtype == torch.bfloat16
+    assert ((ya.float() - ref).norm() / ref.norm()).item() <= GEMM_TOL
+    f = FP8Linear.from_linear(lin)
+    yf = f(x)
+    ref8 = x.float() @ f.dequantize(torch.float16).float().T + lin.bias.float()
+    assert ((yf.float() - ref8).norm() / ref8.norm()).item() <= GEMM_TOL
+
+
+def test_linears_capture_in_cuda_graph():
+    from nanosglang_b200.quantization import AWQLinear, FP8Linear
+    torch.manual_seed(1)
+    lin = nn.Linear(896, 4864, bias=False).cuda().to(torch.bfloat16)
+    a = AWQLinear.from_linear(lin, 128)
+    f = FP8Linear.from_linear(lin)
+    x = torch.randn(16, 896, device="cuda", dtype=torch.bfloat16)
+    xb = torch.randn(256, 896, device="cuda", dtype=torch.bfloat16)
+    eager = (a(x), f(x), a(xb), f(xb))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            a(x), f(x), a(xb), f(xb)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        outs = (a(x), f(x), a(xb), f(xb))
+    g.replay()
+    torch.cuda.synchronize()
+    for e, o in zip(eager, outs):
+        assert torch.equal(e, o)
+
+
+def test_quantize_model_on_cuda():
+    from nanosglang_b200.quantization import AWQLinear, FP8Linear, quantize_model
+    for method, cls in (("awq", AWQLinear), ("fp8", FP8Linear)):
+        m = nn.Sequential()
+        m.add_module("layers", nn.ModuleList([nn.Linear(256, 512), nn.Linear(512, 256)]))
+        m.add_module("lm_head", nn.Linear(256, 100))
+        m = m.cuda()
+        quantize_model(m, method=method, group_size=128)
+        assert isinstance(m.layers[0], cls) and isinstance(m.layers[1], cls)
+        assert isinstance(m.lm_head, nn.Linear)
+        x = torch.randn(3, 256, device="cuda", dtype=torch.float16)
+        assert m.layers[1](m.layers[0](x)).shape == (3, 256)
