@@ -78,38 +78,46 @@ def case_bytes_flops(m, k, n, fmt="fp8", gs=128):
 
 
 class ClockSampler:
+    """nvidia-smi clocks / throttle reasons, sampled every 20 ms from before the
+    timed region starts until after it ends; summary() keeps the samples that
+    fall inside [t0, t1] (the two nearest ones if the region is shorter than
+    the sampling period)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
-        self.samples = []
-        self._stop = threading.Event()
+        self.samples = []  # (host time, fields)
         self._proc = None
         self._thread = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self._proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self._proc = None
             return
         self._thread = threading.Thread(target=self._read, daemon=True)
         self._thread.start()
+        deadline = time.time() + 5.0
+        while not self.samples and time.time() < deadline:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self._proc.stdout:
-            if self._stop.is_set():
-                break
-            parts = [p.strip() for p in line.split(",")]
+            parts = [q.strip() for q in line.split(",")]
             if len(parts) >= 9:
-                self.samples.append(parts)
+                self.samples.append((time.time(), parts))
+
+    def mark(self, which):
+        setattr(self, which, time.time())
 
     def stop(self):
-        self._stop.set()
+        time.sleep(0.05)
         if self._proc is not None:
             self._proc.terminate()
             try:
@@ -118,23 +126,30 @@ class ClockSampler:
                 self._proc.kill()
 
     def summary(self):
-        if not self.samples:
+        if not self.samples or self.t0 is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = []
-        mx = []
+        inside = [p for t, p in self.samples if self.t0 <= t <= self.t1]
+        note = "inside timed region"
+        if not inside:
+            near = sorted(self.samples, key=lambda tp: min(abs(tp[0] - self.t0), abs(tp[0] - self.t1)))[:2]
+            inside = [p for _, p in near]
+            note = "timed region shorter than the 20 ms sampling period: nearest samples"
+        sm, mx, pw = [], [], []
         reasons = set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for p in self.samples:
+        for p in inside:
             try:
                 sm.append(float(p[1]))
                 mx.append(float(p[2]))
+                pw.append(float(p[3]))
             except ValueError:
                 continue
             for name, v in zip(names, p[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "power_w_max": max(pw) if pw else None, "reasons": sorted(reasons), "samples": len(sm),
+                "note": note}
 
 
 # ---------------------------------------------------------------------------
@@ -239,6 +254,9 @@ def run_ours(args):
                                 device_id=device)
     _lib.load()
     _lib.device_status_reset()
+    # weights are written once during set-up and never inside the timed work,
+    # so the linears may start streaming them before the previous kernel ends
+    _lib.set_pdl(not args.no_pdl)
     peaks, peak_src = load_peaks()
 
     cases = build_gpu_cases(torch, ops, device, rank, world)
@@ -278,7 +296,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         if sampler:
-            sampler.start()
+            sampler.mark("t0")
         cur = torch.cuda.current_stream()
         for s, e in evs:
             flush.zero_()
@@ -287,7 +305,7 @@ def run_ours(args):
             e.record(cur)
         torch.cuda.synchronize()
         if sampler:
-            sampler.stop()
+            sampler.mark("t1")
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -301,7 +319,9 @@ def run_ours(args):
     # --- headline: whole step as one graph ---------------------------------
     g_all = capture(cases)
     sampler = ClockSampler(local)
+    sampler.start()
     ms_step = time_graph(g_all, args.steps, args.warmup, sampler)
+    sampler.stop()
     flops_total = sum(2 * c["m"] * c["n"] * c["k"] for c in cases)  # full (unsharded) sweep work
     value = flops_total / (ms_step * 1e-3) / 1e12
 
@@ -397,7 +417,8 @@ def run_ours(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "linears_per_step": len(cases), "weights": "fp8 e4m3, per-tensor scale",
                        "activations": "bf16 N(0,1)", "parallelism": f"tp{world}",
-                       "l2": "flushed between timed steps (256 MiB write)", "timing": "CUDA graph replay, CUDA events"},
+                       "l2": "flushed between timed steps (256 MiB write)", "timing": "CUDA graph replay, CUDA events",
+                       "pdl": not args.no_pdl},
             "roofline": roofline, "decode_kernel": decode_line, "awq_config0": awq, "cpu_baseline": cpu,
             "e2e": e2e, "gpu_launches": len(cases) * args.steps, "clocks": clocks,
         }
@@ -477,6 +498,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle leg")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     out = run_reference(args) if args.impl == "reference" else run_ours(args)

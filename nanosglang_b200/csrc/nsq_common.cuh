@@ -309,17 +309,38 @@ __device__ __forceinline__ void unpack_nibble_pairs(uint32_t w, uint32_t (&e)[4]
   e[3] = lop3_and_or(w >> 12, 0x000F000Fu, M);
 }
 
-// Two e4m3 codes (low byte first) -> packed pair of the MMA element type. Exact.
+// Four e4m3 codes (one word, low byte first) -> two packed pairs of the MMA
+// element type, exact, with integer ops plus one packed multiply per pair
+// (no conversion-pipe instructions). The sign bit goes to bit 15 and the
+// 7-bit exponent|mantissa field lands right below the target exponent field:
+//   bf16: s | em << 4  reads as value * 2^-120,   fp16: s | em << 7  reads as value * 2^-8
+// for every finite code, subnormals included (they land on subnormals of the
+// target type); the packed multiply by 2^120 / 2^8 then restores the value
+// exactly. (NaN codes are not preserved; quantised weights never hold them.)
 template <bool BF16>
-__device__ __forceinline__ uint32_t e4m3x2_to_pair(uint16_t two) {
-  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
+__device__ __forceinline__ void e4m3x4_to_pairs(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t em = w & 0x7F7F7F7Fu;
+  const uint32_t sg = w & 0x80808080u;
+  // per 16-bit lane: (sign byte << 8) | em byte
+  const uint32_t t0 = prmt(em, sg, 0x5140);
+  const uint32_t t1 = prmt(em, sg, 0x7362);
+  constexpr uint32_t kMul = BF16 ? 15u : 127u;  // em + kMul*em = em << 4 (bf16) / << 7 (fp16)
+  const uint32_t r0 = t0 + kMul * (t0 & 0x007F007Fu);
+  const uint32_t r1 = t1 + kMul * (t1 & 0x007F007Fu);
   if constexpr (BF16) {
-    __half2 hh = *reinterpret_cast<__half2*>(&h);
-    float2 f = __half22float2(hh);
-    __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
-    return *reinterpret_cast<uint32_t*>(&b);
+    const uint32_t kbits = 0x7B807B80u;  // {2^120, 2^120}
+    const __nv_bfloat162 k = *reinterpret_cast<const __nv_bfloat162*>(&kbits);
+    __nv_bfloat162 a = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&r0), k);
+    __nv_bfloat162 b = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&r1), k);
+    lo = *reinterpret_cast<uint32_t*>(&a);
+    hi = *reinterpret_cast<uint32_t*>(&b);
   } else {
-    return *reinterpret_cast<uint32_t*>(&h);
+    const uint32_t kbits = 0x5C005C00u;  // {256, 256}
+    const __half2 k = *reinterpret_cast<const __half2*>(&kbits);
+    __half2 a = __hmul2(*reinterpret_cast<const __half2*>(&r0), k);
+    __half2 b = __hmul2(*reinterpret_cast<const __half2*>(&r1), k);
+    lo = *reinterpret_cast<uint32_t*>(&a);
+    hi = *reinterpret_cast<uint32_t*>(&b);
   }
 }
 

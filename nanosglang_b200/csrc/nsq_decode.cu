@@ -5,25 +5,31 @@
 // dequantises the whole weight and calls cuBLAS; here the packed weight is
 // streamed once from HBM and consumed in registers.
 //
-// Design (swap-AB skinny GEMM on the legacy tensor path):
+// Design (swap-AB skinny GEMM on the warp-level tensor path):
 //   * W rows (output features) form the MMA M dimension (16 per warp), tokens
 //     form MMA N (8 per n-tile), so M = 1..64 tokens costs 1..8 n-tiles.
 //   * CTA = 4 warps = 64 output rows x a K slice. Each warp streams its own
-//     16-row strip through a private 8-deep ring of 1 KB TMA tiles taken
-//     straight from the reference layout (qweight [N, K/8] int32 or
-//     weight_fp8 [N, K] uint8) -- no repacked copy of the weight exists.
-//   * AWQ: a 32-bit word of 8 sequential nibbles becomes four packed pairs
+//     16-row strip through a private ring of 1 KB TMA tiles taken straight
+//     from the reference layout (qweight [N, K/8] int32 or weight_fp8 [N, K]
+//     uint8); no repacked copy of the weight exists. All of a CTA's first
+//     tiles are requested before anything else happens.
+//   * x is copied with cp.async (all copies in flight at once, edges
+//     zero-filled) into an XOR-swizzled layout that makes every fragment load
+//     conflict-free.
+//   * AWQ: a word of 8 sequential nibbles becomes four packed pairs
 //     {magic+q_t, magic+q_{t+4}} with one lop3 each (magic = 128 for bf16,
-//     1024 for fp16, exact). The K permutation this implies is applied to x
-//     once per CTA while x is staged into shared memory. Zero points and
-//     scales are applied per 128-column piece in fp32:
-//        y += s * (sum_k (magic+q) x_k - (magic+z) * sum_k x_k),
-//     which is exact algebra for any fp16 zero point.
+//     1024 for fp16; exact). The matching pairs of x are built with prmt.
+//     When every zero point of the CTA is an integer the MMA type represents
+//     exactly with the magic bias (the reference quantiser always produces
+//     those), one packed subtraction gives the exact (q - z); otherwise the
+//     zero point is applied per 128-column piece in fp32 from per-token sums
+//     of x: y += s * (sum (magic+q) x - (magic+z) * sum x).
 //   * FP8: e4m3 pairs convert exactly to the MMA type; the per-tensor scale
 //     is applied once in the epilogue.
-//   * K is split over a thread-block cluster of up to 8 CTAs; partial tiles
-//     are reduced through distributed shared memory (no global workspace),
-//     then bias is added and y is stored coalesced.
+//   * K is split over a thread-block cluster of up to 8 CTAs only when there
+//     are too few row tiles to cover the SMs; partial tiles are reduced
+//     through distributed shared memory (no global workspace). Unsplit CTAs
+//     store straight from registers.
 #include <atomic>
 
 #include "nsq_common.cuh"
@@ -35,22 +41,22 @@ namespace {
 
 constexpr int kWarps = 4;
 constexpr int kRows = 64;          // output rows per CTA
-constexpr int kNst = 8;            // TMA ring depth per warp
+constexpr int kNstMax = 8;         // TMA ring depth per warp (upper bound)
 constexpr int kStageBytes = 1024;  // 16 rows x 64 B
 constexpr int kRedStride = 68;     // fp32 per token row of the partial tile (conflict-free)
+constexpr int kMaxSmem = 200 * 1024;
+constexpr int kXBudget = 48 * 1024;  // bytes for x staging buffers
 
 template <int FMT>
 struct DecFmt;
 template <>
-struct DecFmt<0> {  // AWQ: piece = 128 columns = 64 B per row
+struct DecFmt<0> {  // AWQ: piece = 128 columns = 64 B per weight row
   static constexpr int kPieceK = 128;
-  static constexpr int kXRowBytes = 320;  // 256 B of permuted x + 64 B pad per token
   static constexpr int kChunksPerPiece = 16;
 };
 template <>
-struct DecFmt<1> {  // FP8: piece = 64 columns = 64 B per row
+struct DecFmt<1> {  // FP8: piece = 64 columns = 64 B per weight row
   static constexpr int kPieceK = 64;
-  static constexpr int kXRowBytes = 144;  // 128 B of x + 16 B pad per token
   static constexpr int kChunksPerPiece = 8;
 };
 
@@ -64,119 +70,190 @@ struct DecodeParams {
   DevStatus* status;
   int M, K, N;
   int group_size, G;
-  int k_split;   // columns per CTA (multiple of the piece width)
-  int pmax;      // pieces per CTA (k_split / piece)
-  int ppc;       // pieces per x staging chunk
+  int k_split;  // columns per CTA (multiple of the piece width)
+  int pmax;     // pieces per CTA (k_split / piece)
+  int nst;      // TMA ring depth per warp
+  int ppc;      // pieces per x staging chunk
+  int xrs;      // bytes per token row of an x buffer (ppc * piece * 2)
   int bias_dtype;
   int off_x, off_xsum, off_sz, off_red, off_bar, off_abort;
 };
 
-// Stage x[:, kc0 : kc0 + np*PK) into shared memory (zero-padded past M and K).
-// AWQ: each 8-column chunk is stored permuted [0,4,1,5,2,6,3,7] so that the
-// packed pair t of the chunk holds (x_t, x_{t+4}); per-token piece sums of x
-// go to xsum. FP8: stored in order.
-template <int FMT, bool BF16, int MPAD>
-__device__ __forceinline__ void stage_x(const DecodeParams& p, uint32_t xbuf, float* xsum, int kc0,
-                                        int np, int tid) {
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Position of 16-byte chunk qq (counted along the chunk's columns) of token t.
+// AWQ: XOR bit 0 with bit 3 of qq and bit 1 with the token parity; FP8: XOR
+// bit 0 with the token parity. Both stay inside one piece.
+template <int FMT>
+__device__ __forceinline__ int x_swz(int qq, int t) {
+  if constexpr (FMT == 0) {
+    return qq ^ ((qq >> 3) & 1) ^ ((t & 1) << 1);
+  } else {
+    return qq ^ (t & 1);
+  }
+}
+
+// Issue (without waiting) the copies of x[:, kc0 : kc0 + np*PK) into an x
+// buffer; rows past M and columns past K are zero-filled by the copy itself.
+template <int FMT, int MPAD>
+__device__ __forceinline__ void issue_x_copy(const DecodeParams& p, uint32_t xbuf, int kc0, int np,
+                                             int tid) {
   using F = DecFmt<FMT>;
-  const int total = np * MPAD * F::kChunksPerPiece;
+  const int cpr = np * F::kChunksPerPiece;  // 16-byte chunks per token row
+  const int total = MPAD * cpr;
   const uint16_t* x = static_cast<const uint16_t*>(p.x);
+  for (int idx = tid; idx < total; idx += kWarps * 32) {
+    const int t = idx / cpr;
+    const int q = idx - t * cpr;
+    const int k = kc0 + q * 8;
+    const bool valid = t < p.M && k < p.K;
+    const uint16_t* src = valid ? x + (int64_t)t * p.K + k : x;
+    cp_async16(xbuf + t * p.xrs + x_swz<FMT>(q, t) * 16, src, valid ? 16u : 0u);
+  }
+}
+
+// AWQ general path: per-token sums of x over each 128-column piece (fp32).
+template <bool BF16, int MPAD>
+__device__ __forceinline__ void piece_sums(const DecodeParams& p, uint32_t xbuf, float* xsum, int np,
+                                           int tid) {
+  constexpr int CPP = DecFmt<0>::kChunksPerPiece;
+  const int total = np * MPAD * CPP;
   for (int base = 0; base < total; base += kWarps * 32) {
     const int item = base + tid;
     const bool valid = item < total;
-    const int q = item % F::kChunksPerPiece;
-    const int pt = item / F::kChunksPerPiece;  // jl * MPAD + t
+    const int q = item % CPP;
+    const int pt = item / CPP;  // jl * MPAD + t
     const int t = pt % MPAD;
     const int jl = pt / MPAD;
-    const int k = kc0 + jl * F::kPieceK + q * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (valid && t < p.M && k < p.K) {
-      v = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)t * p.K + k));
-    }
-    if constexpr (FMT == 0) {
-      // piece sum of x for this token (16 chunks = one half-warp)
+    float s = 0.f;
+    if (valid) {
+      const uint4 v = lds128(xbuf + t * p.xrs + x_swz<0>(jl * CPP + q, t) * 16);
       const uint32_t r[4] = {v.x, v.y, v.z, v.w};
-      float s = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         s += elem_to_float<BF16>(static_cast<uint16_t>(r[i] & 0xFFFFu));
         s += elem_to_float<BF16>(static_cast<uint16_t>(r[i] >> 16));
       }
-      s += __shfl_xor_sync(0xffffffffu, s, 8);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      if (valid) {
-        if (q == 0) xsum[pt] = s;
-        const uint32_t p0 = prmt(v.x, v.z, 0x5410), p1 = prmt(v.x, v.z, 0x7632);
-        const uint32_t p2 = prmt(v.y, v.w, 0x5410), p3 = prmt(v.y, v.w, 0x7632);
-        const int cq = q >> 2, iq = q & 3;
-        sts128(xbuf + pt * F::kXRowBytes + iq * 64 + cq * 16, p0, p1, p2, p3);
-      }
-    } else {
-      if (valid) sts128(xbuf + pt * F::kXRowBytes + q * 16, v.x, v.y, v.z, v.w);
     }
+    s += __shfl_xor_sync(0xffffffffu, s, 8);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (valid && q == 0) xsum[pt] = s;
   }
 }
 
-template <bool BF16, int MT>
+template <bool BF16>
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 r = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                               *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  } else {
+    __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack_pair(float v) {
+  if constexpr (BF16) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(v, v);
+    return *reinterpret_cast<uint32_t*>(&b);
+  } else {
+    __half2 h = __floats2half2_rn(v, v);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// One 128-column piece of one warp's 16 rows (AWQ). INT_Z: exact integer zero
+// points subtracted in the packed domain; else the fp32 fold with x sums.
+template <bool BF16, int MT, bool INT_Z>
 __device__ __forceinline__ void awq_piece(float (&acc)[MT][4], const uint4& wa, const uint4& wb,
-                                          uint32_t xpiece, const float* xs, float s0, float z0,
-                                          float s1, float z1, int g, int c) {
+                                          uint32_t xrow0, int xrs, const float* xs, float s0, float zb0,
+                                          float s1, float zb1, int g, int c) {
   float part[MT][4];
 #pragma unroll
   for (int jt = 0; jt < MT; ++jt) part[jt][0] = part[jt][1] = part[jt][2] = part[jt][3] = 0.f;
   const uint32_t wg[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t wh[4] = {wb.x, wb.y, wb.z, wb.w};
+  uint32_t z2g = 0, z2h = 0;
+  if constexpr (INT_Z) {
+    z2g = pack_pair<BF16>(zb0);
+    z2h = pack_pair<BF16>(zb1);
+  }
+  const int m = (c >> 1) | ((g & 1) << 1);  // swizzle of this thread's chunks
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     uint32_t eg[4], eh[4];
     unpack_nibble_pairs<BF16>(wg[i], eg);
     unpack_nibble_pairs<BF16>(wh[i], eh);
-    uint4 xv[MT];
+    if constexpr (INT_Z) {
 #pragma unroll
-    for (int jt = 0; jt < MT; ++jt) {
-      xv[jt] = lds128(xpiece + (8 * jt + g) * DecFmt<0>::kXRowBytes + i * 64 + c * 16);
+      for (int t = 0; t < 4; ++t) {
+        eg[t] = hsub2_bits<BF16>(eg[t], z2g);
+        eh[t] = hsub2_bits<BF16>(eh[t], z2h);
+      }
     }
     const uint32_t a0[4] = {eg[0], eh[0], eg[1], eh[1]};
-#pragma unroll
-    for (int jt = 0; jt < MT; ++jt) mma_16816<BF16>(part[jt], a0, xv[jt].x, xv[jt].y);
     const uint32_t a1[4] = {eg[2], eh[2], eg[3], eh[3]};
 #pragma unroll
-    for (int jt = 0; jt < MT; ++jt) mma_16816<BF16>(part[jt], a1, xv[jt].z, xv[jt].w);
+    for (int jt = 0; jt < MT; ++jt) {
+      // x[8jt+g][32c + 8i .. +7] -> pairs (x_t, x_{t+4})
+      const uint4 v = lds128(xrow0 + (8 * jt + g) * xrs + (4 * c + (i ^ m)) * 16);
+      const uint32_t p0 = prmt(v.x, v.z, 0x5410), p1 = prmt(v.x, v.z, 0x7632);
+      const uint32_t p2 = prmt(v.y, v.w, 0x5410), p3 = prmt(v.y, v.w, 0x7632);
+      mma_16816<BF16>(part[jt], a0, p0, p1);
+      mma_16816<BF16>(part[jt], a1, p2, p3);
+    }
   }
 #pragma unroll
   for (int jt = 0; jt < MT; ++jt) {
-    const float xa = xs[8 * jt + 2 * c], xb = xs[8 * jt + 2 * c + 1];
-    acc[jt][0] = fmaf(s0, fmaf(-z0, xa, part[jt][0]), acc[jt][0]);
-    acc[jt][1] = fmaf(s0, fmaf(-z0, xb, part[jt][1]), acc[jt][1]);
-    acc[jt][2] = fmaf(s1, fmaf(-z1, xa, part[jt][2]), acc[jt][2]);
-    acc[jt][3] = fmaf(s1, fmaf(-z1, xb, part[jt][3]), acc[jt][3]);
+    if constexpr (INT_Z) {
+      acc[jt][0] = fmaf(s0, part[jt][0], acc[jt][0]);
+      acc[jt][1] = fmaf(s0, part[jt][1], acc[jt][1]);
+      acc[jt][2] = fmaf(s1, part[jt][2], acc[jt][2]);
+      acc[jt][3] = fmaf(s1, part[jt][3], acc[jt][3]);
+    } else {
+      const float xa = xs[8 * jt + 2 * c], xb = xs[8 * jt + 2 * c + 1];
+      acc[jt][0] = fmaf(s0, fmaf(-zb0, xa, part[jt][0]), acc[jt][0]);
+      acc[jt][1] = fmaf(s0, fmaf(-zb0, xb, part[jt][1]), acc[jt][1]);
+      acc[jt][2] = fmaf(s1, fmaf(-zb1, xa, part[jt][2]), acc[jt][2]);
+      acc[jt][3] = fmaf(s1, fmaf(-zb1, xb, part[jt][3]), acc[jt][3]);
+    }
   }
 }
 
 template <bool BF16, int MT>
 __device__ __forceinline__ void fp8_piece(float (&acc)[MT][4], const uint4& wa, const uint4& wb,
-                                          uint32_t xpiece, int g, int c) {
+                                          uint32_t xrow0, int xrs, int g, int c) {
   const uint32_t wg[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t wh[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-  for (int i = 0; i < 4; i += 2) {
+  for (int h = 0; h < 2; ++h) {
     uint4 xv[MT];
 #pragma unroll
     for (int jt = 0; jt < MT; ++jt) {
-      xv[jt] = lds128(xpiece + (8 * jt + g) * DecFmt<1>::kXRowBytes + (16 * c + 4 * i) * 2);
+      // x[8jt+g][16c + 8h .. +7]
+      xv[jt] = lds128(xrow0 + (8 * jt + g) * xrs + (2 * c + (h ^ (g & 1))) * 16);
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int s = i + h;
-      const uint32_t a[4] = {e4m3x2_to_pair<BF16>(static_cast<uint16_t>(wg[s] & 0xFFFFu)),
-                             e4m3x2_to_pair<BF16>(static_cast<uint16_t>(wh[s] & 0xFFFFu)),
-                             e4m3x2_to_pair<BF16>(static_cast<uint16_t>(wg[s] >> 16)),
-                             e4m3x2_to_pair<BF16>(static_cast<uint16_t>(wh[s] >> 16))};
+    for (int u = 0; u < 2; ++u) {
+      const int s = 2 * h + u;
+      uint32_t a[4];
+      e4m3x4_to_pairs<BF16>(wg[s], a[0], a[2]);
+      e4m3x4_to_pairs<BF16>(wh[s], a[1], a[3]);
 #pragma unroll
       for (int jt = 0; jt < MT; ++jt) {
-        mma_16816<BF16>(acc[jt], a, h ? xv[jt].z : xv[jt].x, h ? xv[jt].w : xv[jt].y);
+        mma_16816<BF16>(acc[jt], a, u ? xv[jt].z : xv[jt].x, u ? xv[jt].w : xv[jt].y);
       }
     }
   }
@@ -196,55 +273,79 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
   const int k_begin = rank * p.k_split;
   const int k_end = min(p.K, k_begin + p.k_split);
   const int P = (k_end - k_begin + F::kPieceK - 1) / F::kPieceK;
+  const int nst = p.nst;
 
   const uint32_t wring = smem_u32(smem);
-  const uint32_t xbuf = smem_u32(smem + p.off_x);
+  const uint32_t xbuf0 = smem_u32(smem + p.off_x);
   float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);
   float* sz = reinterpret_cast<float*>(smem + p.off_sz);
   float* red = reinterpret_cast<float*>(smem + p.off_red);
-  uint64_t* wbar = reinterpret_cast<uint64_t*>(smem + p.off_bar) + warp * kNst;
+  uint64_t* bar_base = reinterpret_cast<uint64_t*>(smem + p.off_bar);
+  uint64_t* wbar = bar_base + warp * kNstMax;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.off_abort);
+  const int xbuf_bytes = MPAD * p.xrs;
 
-  if (tid == 0) *abort_flag = 0;
-  if (lane == 0) {
-    for (int s = 0; s < kNst; ++s) mbar_init(&wbar[s], 1);
+  if (tid == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < kWarps * kNstMax; ++s) mbar_init(bar_base + s, 1);
     fence_barrier_init();
   }
-  __syncwarp();
+  __syncthreads();
 
   auto issue = [&](int j) {
-    const int buf = j % kNst;
+    const int buf = j % nst;
     mbar_arrive_expect_tx(&wbar[buf], kStageBytes);
     const int kk = k_begin + j * F::kPieceK;
-    tma_load_2d(smem + (warp * kNst + buf) * kStageBytes, &wmap, &wbar[buf],
+    tma_load_2d(smem + (warp * kNstMax + buf) * kStageBytes, &wmap, &wbar[buf],
                 FMT == 0 ? kk / 8 : kk, n0 + 16 * warp);
   };
   int issued = 0;
   if (lane == 0) {
-    tma_prefetch_desc(&wmap);
-    const int first = P < kNst ? P : kNst;
+    const int first = P < nst ? P : nst;
     for (int j = 0; j < first; ++j) issue(j);
     issued = first;
   }
 
+  bool int_zeros = true;
   if constexpr (FMT == 0) {
-    // per-piece scale and biased zero point of this CTA's 64 rows (fp32)
-    for (int idx = tid; idx < P * kRows; idx += kWarps * 32) {
-      const int j = idx / kRows, r = idx % kRows;
-      const int n = n0 + r;
-      const int grp = (k_begin + j * F::kPieceK) / p.group_size;
-      float s = 0.f, zb = 0.f;
-      if (n < p.N) {
-        s = __half2float(p.scales[(int64_t)n * p.G + grp]);
-        zb = Magic<BF16>::kValue + __half2float(p.zeros[(int64_t)n * p.G + grp]);
+    // per-piece scale and biased zero point of this CTA's 64 rows (fp32);
+    // loads are batched so their latencies overlap
+    constexpr float kZMax = BF16 ? 127.0f : 1023.0f;
+    const int total = P * kRows;
+    bool all_int = true;
+    for (int base = 0; base < total; base += kWarps * 32 * 8) {
+      float sv[8], zv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = base + tid + kWarps * 32 * u;
+        const int j = idx / kRows, r = idx % kRows;
+        const int n = n0 + r;
+        sv[u] = 0.f;
+        zv[u] = 0.f;
+        if (idx < total && n < p.N) {
+          const int64_t off = (int64_t)n * p.G + (k_begin + j * F::kPieceK) / p.group_size;
+          sv[u] = __half2float(p.scales[off]);
+          zv[u] = __half2float(p.zeros[off]);
+        }
       }
-      sz[j * kRows + r] = s;
-      sz[(p.pmax + j) * kRows + r] = zb;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = base + tid + kWarps * 32 * u;
+        if (idx < total) {
+          const int j = idx / kRows, r = idx % kRows;
+          sz[j * kRows + r] = sv[u];
+          sz[(p.pmax + j) * kRows + r] = Magic<BF16>::kValue + zv[u];
+          all_int = all_int && (zv[u] == rintf(zv[u])) && fabsf(zv[u]) <= kZMax;
+        }
+      }
     }
+    int_zeros = __syncthreads_and(all_int ? 1 : 0) != 0;
   }
 
-  // x and bias may be produced by the previous kernel on the stream
+  // x (and bias) may be produced by the previous kernel on the stream; from
+  // here on the next kernel may start streaming its own weights
   pdl_wait_prior_grids();
+  pdl_launch_dependents();
 
   float acc[MT][4];
 #pragma unroll
@@ -253,84 +354,121 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
   bool ok = true;
   int consumed = 0;
   const int nchunks = (P + p.ppc - 1) / p.ppc;
+  // x chunks double-buffered: the copy of chunk ch+1 flies while chunk ch computes
+  issue_x_copy<FMT, MPAD>(p, xbuf0, k_begin, min(P, p.ppc), tid);
+  cp_async_commit();
   for (int ch = 0; ch < nchunks; ++ch) {
     const int j0 = ch * p.ppc;
     const int j1 = min(P, j0 + p.ppc);
-    __syncthreads();  // previous chunk fully consumed (and sz/abort init visible)
-    stage_x<FMT, BF16, MPAD>(p, xbuf, xsum, k_begin + j0 * F::kPieceK, j1 - j0, tid);
-    __syncthreads();
+    const uint32_t xb = xbuf0 + (ch & 1) * xbuf_bytes;
+    if (ch + 1 < nchunks) {
+      const int n1 = min(P, j1 + p.ppc) - j1;
+      issue_x_copy<FMT, MPAD>(p, xbuf0 + ((ch + 1) & 1) * xbuf_bytes, k_begin + j1 * F::kPieceK, n1, tid);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // chunk ch landed for every thread
+    if constexpr (FMT == 0) {
+      if (!int_zeros) {
+        piece_sums<BF16, MPAD>(p, xb, xsum, j1 - j0, tid);
+        __syncthreads();
+      }
+    }
     for (int j = j0; j < j1; ++j) {
-      const int buf = j % kNst;
-      if (ok) ok = mbar_wait(&wbar[buf], (j / kNst) & 1, p.status, 1, abort_flag);
+      const int buf = j % nst;
+      if (ok) ok = mbar_wait(&wbar[buf], (j / nst) & 1, p.status, 1, abort_flag);
       if (ok) {
-        const uint32_t wt = wring + (warp * kNst + buf) * kStageBytes;
+        const uint32_t wt = wring + (warp * kNstMax + buf) * kStageBytes;
         const uint4 wa = lds128(wt + g * 64 + c * 16);
         const uint4 wb = lds128(wt + (g + 8) * 64 + c * 16);
         const int jl = j - j0;
-        const uint32_t xpiece = xbuf + jl * MPAD * F::kXRowBytes;
+        const uint32_t xrow0 = xb + jl * F::kPieceK * 2;
         if constexpr (FMT == 0) {
           const int r0 = 16 * warp + g;
-          awq_piece<BF16, MT>(acc, wa, wb, xpiece, xsum + jl * MPAD, sz[j * kRows + r0],
-                              sz[(p.pmax + j) * kRows + r0], sz[j * kRows + r0 + 8],
-                              sz[(p.pmax + j) * kRows + r0 + 8], g, c);
+          const float s0 = sz[j * kRows + r0], s1 = sz[j * kRows + r0 + 8];
+          const float zb0 = sz[(p.pmax + j) * kRows + r0], zb1 = sz[(p.pmax + j) * kRows + r0 + 8];
+          if (int_zeros) {
+            awq_piece<BF16, MT, true>(acc, wa, wb, xrow0, p.xrs, nullptr, s0, zb0, s1, zb1, g, c);
+          } else {
+            awq_piece<BF16, MT, false>(acc, wa, wb, xrow0, p.xrs, xsum + jl * MPAD, s0, zb0, s1, zb1, g, c);
+          }
         } else {
-          fp8_piece<BF16, MT>(acc, wa, wb, xpiece, g, c);
+          fp8_piece<BF16, MT>(acc, wa, wb, xrow0, p.xrs, g, c);
         }
         consumed = j + 1;
       }
       __syncwarp();
-      if (lane == 0 && ok && j + kNst < P) {
-        issue(j + kNst);
-        issued = j + kNst + 1;
+      if (lane == 0 && ok && j + nst < P) {
+        issue(j + nst);
+        issued = j + nst + 1;
       }
     }
+    if (ch + 1 < nchunks) __syncthreads();  // every warp is done with this x buffer
   }
-  pdl_launch_dependents();
 
-  // partial tile -> shared memory, [token][row]
-#pragma unroll
-  for (int jt = 0; jt < MT; ++jt) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int tok = 8 * jt + 2 * c + (e & 1);
-      const int row = 16 * warp + g + 8 * (e >> 1);
-      red[tok * kRedStride + row] = acc[jt][e];
-    }
-  }
-  if (S > 1) {
-    cluster_sync_all();
-  } else {
-    __syncthreads();
-  }
-  const int E = p.M * kRows;
-  const int per = (E + S - 1) / S;
-  const int e0 = rank * per;
-  const int e1 = min(E, e0 + per);
   const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
   uint16_t* y = static_cast<uint16_t*>(p.y);
-  for (int e = e0 + tid; e < e1; e += kWarps * 32) {
-    const int tok = e / kRows, row = e % kRows;
-    const int n = n0 + row;
-    if (n >= p.N) continue;
-    const uint32_t la = smem_u32(&red[tok * kRedStride + row]);
-    float v = 0.f;
-    for (int r = 0; r < S; ++r) v += (r == rank) ? red[tok * kRedStride + row] : dsmem_ld_f32(dsmem_map(la, r));
-    v *= wscale;
-    if (p.bias_dtype != NSQ_DTYPE_NONE) v += load_bias(p.bias, p.bias_dtype, n);
-    y[(int64_t)tok * p.N + n] = float_to_elem<BF16>(v);
+  if (S == 1) {
+    // unsplit: scale, bias and store straight from the accumulators
+    const int ra = n0 + 16 * warp + g, rb = ra + 8;
+    float ba = 0.f, bb = 0.f;
+    if (p.bias_dtype != NSQ_DTYPE_NONE) {
+      if (ra < p.N) ba = load_bias(p.bias, p.bias_dtype, ra);
+      if (rb < p.N) bb = load_bias(p.bias, p.bias_dtype, rb);
+    }
+#pragma unroll
+    for (int jt = 0; jt < MT; ++jt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = 8 * jt + 2 * c + (e & 1);
+        const int n = (e >> 1) ? rb : ra;
+        if (tok < p.M && n < p.N) {
+          y[(int64_t)tok * p.N + n] = float_to_elem<BF16>(fmaf(acc[jt][e], wscale, (e >> 1) ? bb : ba));
+        }
+      }
+    }
+  } else {
+    // partial tile -> shared memory [token][row], reduced across the cluster
+#pragma unroll
+    for (int jt = 0; jt < MT; ++jt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = 8 * jt + 2 * c + (e & 1);
+        const int row = 16 * warp + g + 8 * (e >> 1);
+        red[tok * kRedStride + row] = acc[jt][e];
+      }
+    }
+    cluster_sync_all();
+    const int E = p.M * kRows;
+    const int per = (E + S - 1) / S;
+    const int e0 = rank * per;
+    const int e1 = min(E, e0 + per);
+    for (int e = e0 + tid; e < e1; e += kWarps * 32) {
+      const int tok = e / kRows, row = e % kRows;
+      const int n = n0 + row;
+      if (n >= p.N) continue;
+      const uint32_t la = smem_u32(&red[tok * kRedStride + row]);
+      float v = 0.f;
+      for (int r = 0; r < S; ++r) v += (r == rank) ? red[tok * kRedStride + row] : dsmem_ld_f32(dsmem_map(la, r));
+      v *= wscale;
+      if (p.bias_dtype != NSQ_DTYPE_NONE) v += load_bias(p.bias, p.bias_dtype, n);
+      y[(int64_t)tok * p.N + n] = float_to_elem<BF16>(v);
+    }
+    cluster_sync_all();
   }
-  if (S > 1) cluster_sync_all();
 
   // after an abort, let this warp's outstanding copies land before exiting
   if (lane == 0 && !ok) {
     for (int j = consumed; j < issued; ++j) {
-      mbar_wait(&wbar[j % kNst], (j / kNst) & 1, nullptr, 0, nullptr);
+      mbar_wait(&wbar[j % nst], (j / nst) & 1, nullptr, 0, nullptr);
     }
   }
 }
 
 struct Plan {
-  int S, k_split, pmax, ppc;
+  int S, k_split, pmax, nst, ppc, xrs;
   size_t smem;
   int off_x, off_xsum, off_sz, off_red, off_bar, off_abort;
 };
@@ -343,7 +481,8 @@ Plan make_plan(int M, int K, int N) {
   const int pieces = (K + F::kPieceK - 1) / F::kPieceK;
   const int rt = (N + kRows - 1) / kRows;
   const int sms = num_sms();
-  int S = (2 * sms + rt - 1) / rt;
+  // split K only as far as needed to put a CTA on every SM
+  int S = (sms + rt - 1) / rt;
   S = S < 1 ? 1 : S;
   S = S > 8 ? 8 : S;
   S = S > pieces ? pieces : S;
@@ -353,22 +492,32 @@ Plan make_plan(int M, int K, int N) {
   pl.S = S;
   pl.pmax = per;
   pl.k_split = per * F::kPieceK;
-  int ppc = 40960 / (mpad * F::kXRowBytes);
-  ppc = ppc < 1 ? 1 : ppc;
-  pl.ppc = ppc > per ? per : ppc;
-  size_t off = (size_t)kWarps * kNst * kStageBytes;
+  pl.nst = per < kNstMax ? per : kNstMax;
+  // x staging: one buffer for the whole slice if it fits, else two chunk buffers
+  const int piece_token_bytes = F::kPieceK * 2;
+  int nbuf;
+  if ((size_t)per * piece_token_bytes * mpad <= (size_t)kXBudget) {
+    pl.ppc = per;
+    nbuf = 1;
+  } else {
+    int ppc = kXBudget / (2 * mpad * piece_token_bytes);
+    pl.ppc = ppc < 1 ? 1 : ppc;
+    nbuf = 2;
+  }
+  pl.xrs = pl.ppc * piece_token_bytes;
+  size_t off = (size_t)kWarps * kNstMax * kStageBytes;
   pl.off_x = (int)off;
-  off += (size_t)mpad * pl.ppc * F::kXRowBytes;
+  off += (size_t)nbuf * mpad * pl.xrs;
   pl.off_xsum = (int)off;
   off += (FMT == 0) ? (size_t)mpad * pl.ppc * 4 : 0;
   pl.off_sz = (int)off;
   off += (FMT == 0) ? (size_t)2 * per * kRows * 4 : 0;
   off = (off + 15) & ~(size_t)15;
   pl.off_red = (int)off;
-  off += (size_t)mpad * kRedStride * 4;
+  off += (S > 1) ? (size_t)mpad * kRedStride * 4 : 0;
   off = (off + 7) & ~(size_t)7;
   pl.off_bar = (int)off;
-  off += (size_t)kWarps * kNst * 8;
+  off += (size_t)kWarps * kNstMax * 8;
   pl.off_abort = (int)off;
   off += 16;
   pl.smem = off;
@@ -379,13 +528,16 @@ template <int FMT, bool BF16, int MT>
 cudaError_t launch_t(const CUtensorMap& map, const DecodeParams& p, const Plan& pl,
                      cudaStream_t stream) {
   auto kern = decode_linear_kernel<FMT, BF16, MT>;
-  static std::atomic<size_t> configured{0};
-  if (configured.load() < pl.smem) {
+  // one fixed cap for every plan, set on first use (a warm-up call before any
+  // graph capture takes care of it)
+  static std::atomic<bool> configured{false};
+  if (!configured.load()) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)pl.smem);
+                                         kMaxSmem);
     if (e != cudaSuccess) return e;
-    configured.store(pl.smem);
+    configured.store(true);
   }
+  if (pl.smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.S, (p.N + kRows - 1) / kRows, 1);
   cfg.blockDim = dim3(kWarps * 32, 1, 1);
@@ -459,7 +611,9 @@ int run_decode_linear(const LinearArgs& a, cudaStream_t stream) {
   p.G = a.fmt == 0 ? (a.K + a.group_size - 1) / a.group_size : 0;
   p.k_split = pl.k_split;
   p.pmax = pl.pmax;
+  p.nst = pl.nst;
   p.ppc = pl.ppc;
+  p.xrs = pl.xrs;
   p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
   p.off_x = pl.off_x;
   p.off_xsum = pl.off_xsum;

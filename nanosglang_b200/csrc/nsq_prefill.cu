@@ -260,25 +260,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
     // ---------------- converters: one weight row per thread ----------------
     const int row = (warp - kWarpConv0) * 32 + lane;  // 0..255
     int it_l = 0, it_b = 0;
-    int cached_group = -1, cached_n = -1;
     AwqRowParams<BF16> rp{};
+    // AWQ: raw fp16 (scale, zero) of the k-block about to be converted, loaded
+    // one k-block ahead so the global-load latency hides behind a conversion
+    const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
+    const unsigned short* zr16 = reinterpret_cast<const unsigned short*>(p.zeros);
+    auto fetch_sz = [&](int tile, int kb, unsigned short& s16, unsigned short& z16) {
+      s16 = 0;
+      z16 = 0;
+      if (tile < num_tiles) {
+        const int n = (tile % p.num_n_tiles) * BN + row;
+        if (n < p.N) {
+          const int64_t off = (int64_t)n * p.G + (kb * BK) / p.group_size;
+          s16 = __ldg(sc16 + off);
+          z16 = __ldg(zr16 + off);
+        }
+      }
+    };
+    unsigned short cur_s = 0, cur_z = 0;
+    if constexpr (FMT == 0) fetch_sz(blockIdx.x, 0, cur_s, cur_z);
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const int nt = tile % p.num_n_tiles;
-      const int n = nt * BN + row;
       for (int kb = 0; kb < p.num_kb; ++kb, ++it_l, ++it_b) {
         const int sl = it_l % NL, sb = it_b % NB;
         if constexpr (FMT == 0) {
-          const int grp = (kb * BK) / p.group_size;
-          if (grp != cached_group || n != cached_n) {
-            float s = 0.f, z = 0.f;
-            if (n < p.N) {
-              s = __half2float(p.scales[(int64_t)n * p.G + grp]);
-              z = __half2float(p.zeros[(int64_t)n * p.G + grp]);
-            }
-            rp = awq_row_params<BF16>(s, z);
-            cached_group = grp;
-            cached_n = n;
+          unsigned short nxt_s, nxt_z;
+          if (kb + 1 < p.num_kb) {
+            fetch_sz(tile, kb + 1, nxt_s, nxt_z);
+          } else {
+            fetch_sz(tile + gridDim.x, 0, nxt_s, nxt_z);
           }
+          if (kb == 0 || (kb * BK) % p.group_size == 0) {
+            rp = awq_row_params<BF16>(__half2float(__ushort_as_half(cur_s)),
+                                      __half2float(__ushort_as_half(cur_z)));
+          }
+          cur_s = nxt_s;
+          cur_z = nxt_z;
         }
         if (!(ok = mbar_wait(&full_l[sl], (it_l / NL) & 1, p.status, 30, abort_flag))) break;
         if (!(ok = mbar_wait(&empty_b[sb], ((it_b / NB) & 1) ^ 1, p.status, 31, abort_flag))) break;
@@ -308,15 +324,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
 #pragma unroll
           for (int cch = 0; cch < 4; ++cch) {
             const uint4 v = lds128(wc + ((cch ^ sw) << 4));
-            const uint32_t o0 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.x & 0xFFFFu));
-            const uint32_t o1 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.x >> 16));
-            const uint32_t o2 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.y & 0xFFFFu));
-            const uint32_t o3 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.y >> 16));
+            uint32_t o0, o1, o2, o3, o4, o5, o6, o7;
+            e4m3x4_to_pairs<BF16>(v.x, o0, o1);
+            e4m3x4_to_pairs<BF16>(v.y, o2, o3);
+            e4m3x4_to_pairs<BF16>(v.z, o4, o5);
+            e4m3x4_to_pairs<BF16>(v.w, o6, o7);
             sts128(brow + (((2 * cch) ^ (row & 7)) << 4), o0, o1, o2, o3);
-            const uint32_t o4 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.z & 0xFFFFu));
-            const uint32_t o5 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.z >> 16));
-            const uint32_t o6 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.w & 0xFFFFu));
-            const uint32_t o7 = e4m3x2_to_pair<BF16>(static_cast<uint16_t>(v.w >> 16));
             sts128(brow + (((2 * cch + 1) ^ (row & 7)) << 4), o4, o5, o6, o7);
           }
         }

@@ -350,3 +350,20 @@ def test_quantize_model_on_cuda():
         assert isinstance(m.lm_head, nn.Linear)
         x = torch.randn(3, 256, device="cuda", dtype=torch.float16)
         assert m.layers[1](m.layers[0](x)).shape == (3, 256)
+
+
+@pytest.mark.parametrize("m", [4, 40, 200])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fp8_linear_every_code(m, dtype):
+    """Weights cycling through all 254 finite e4m3 codes (subnormals and signed
+    zero included) through the in-register conversion of both kernels."""
+    from nanosglang_b200 import ops
+    n, k = 96, 512
+    codes = (np.arange(n * k, dtype=np.int64) * 7 % 256).astype(np.uint8).reshape(n, k)
+    codes[(codes & 0x7F) == 0x7F] = 0x01  # no NaN codes
+    scale = np.float32(0.01)
+    x = rand_x(m, k, dtype, seed=m)
+    y = ops.fp8_linear(x.cuda(), torch.from_numpy(codes).cuda().view(torch.float8_e4m3fn),
+                       torch.tensor(scale).cuda())
+    ref = O.fp8_linear(_to_np(x), codes, scale)
+    assert O.rel_fro(_to_np(y), ref) <= GEMM_TOL
