@@ -176,6 +176,7 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
 static int linear_common(LinearArgs& a, cudaStream_t stream) {
   if (a.M == 0) return NSQ_OK;
   if (a.M <= kDecodeMaxM) return run_decode_linear(a, stream);
+  if (pair_prefill_supported(a)) return run_prefill_pair_linear(a, stream);
   return run_prefill_linear(a, stream);
 }
 

@@ -48,7 +48,9 @@ struct LinearArgs {
   void* y;
 };
 int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64
-int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M
+int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M, one CTA per tile
+bool pair_prefill_supported(const LinearArgs& a);
+int run_prefill_pair_linear(const LinearArgs& a, cudaStream_t stream);  // M > 128, CTA pairs
 
 constexpr int kDecodeMaxM = 64;
 

@@ -107,6 +107,17 @@ __device__ __forceinline__ uint32_t pack2(float v) {
 }
 
 template <bool BF16>
+__device__ __forceinline__ uint32_t pack2_rn(float a, float b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <bool BF16>
 __device__ __forceinline__ AwqRowParams<BF16> awq_row_params(float s, float z) {
   AwqRowParams<BF16> r;
   constexpr float kMagic = Magic<BF16>::kValue;
@@ -362,16 +373,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
         tmem_ld_32x32b_x32(taddr + cc * 32, r);
         tmem_ld_wait();
         const int nb = nt * BN + cc * 32;
-        float bl = 0.f;
-        if (p.bias_dtype != NSQ_DTYPE_NONE && nb + lane < p.N) bl = load_bias(p.bias, p.bias_dtype, nb + lane);
         uint32_t o[16];
+        if (p.bias_dtype != NSQ_DTYPE_NONE) {
+          const float bl = (nb + lane < p.N) ? load_bias(p.bias, p.bias_dtype, nb + lane) : 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float b0 = __shfl_sync(0xffffffffu, bl, 2 * i);
-          const float b1 = __shfl_sync(0xffffffffu, bl, 2 * i + 1);
-          const float v0 = fmaf(__uint_as_float(r[2 * i]), wscale, b0);
-          const float v1 = fmaf(__uint_as_float(r[2 * i + 1]), wscale, b1);
-          o[i] = (uint32_t)float_to_elem<BF16>(v0) | ((uint32_t)float_to_elem<BF16>(v1) << 16);
+          for (int i = 0; i < 16; ++i) {
+            const float b0 = __shfl_sync(0xffffffffu, bl, 2 * i);
+            const float b1 = __shfl_sync(0xffffffffu, bl, 2 * i + 1);
+            o[i] = pack2_rn<BF16>(fmaf(__uint_as_float(r[2 * i]), wscale, b0),
+                                  fmaf(__uint_as_float(r[2 * i + 1]), wscale, b1));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            o[i] = pack2_rn<BF16>(__uint_as_float(r[2 * i]) * wscale, __uint_as_float(r[2 * i + 1]) * wscale);
+          }
         }
         if (m < p.M) {
           uint16_t* dst = y + (int64_t)m * p.N + nb;
