@@ -124,6 +124,20 @@ size_t nsq_fp8_quantize_workspace_size(int64_t N, int64_t K);
 int nsq_fp8_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* weight_fp8,
                      float* weight_scale, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free FP8 quantiser: the same result as nsq_fp8_quantize, but the
+ * absmax scratch comes from a 256-byte array inside the library instead of a
+ * caller workspace. No counterpart in the reference. For callers that cannot
+ * allocate device memory when they quantise (inside a global-mode stream
+ * capture, engines whose HBM is pre-reserved for the KV cache, C callers with
+ * no device allocator). Returns NSQ_EWORKSPACE if a shape would need more
+ * scratch than the array holds. Calls share the array: calls that overlap on
+ * the GPU race, so serialise them. The first call on a device looks up the
+ * array's device address; make it before any stream capture begins.
+ */
+int nsq_fp8_quantize_noalloc(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* weight_fp8,
+                             float* weight_scale, void* stream);
+
 /* Opt in (1) or out (0, default) of programmatic dependent launch for the
  * linear kernels: with it on, a linear starts streaming its weights while the
  * previous kernel on the stream drains. Only valid when no kernel earlier on

@@ -50,6 +50,7 @@ SIGNATURES = {
     "nsq_fp8_quantize_workspace_size": (c_size_t, [c_int64, c_int64]),
     "nsq_fp8_quantize": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_size_t,
                                  c_void_p]),
+    "nsq_fp8_quantize_noalloc": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "nsq_set_pdl": (c_int, [c_int]),
 }
 

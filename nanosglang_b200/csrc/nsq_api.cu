@@ -83,6 +83,8 @@ DevStatus* device_status_ptr() {
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
+int device_ready() { return check_device(); }
+
 CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
                               uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {

@@ -11,6 +11,7 @@ namespace nsq {
 struct DevStatus;
 
 int num_sms();                  // SM count of the current device (cached per device)
+int device_ready();             // NSQ_OK if the current device is sm_100, else an NSQ_E* code
 DevStatus* device_status_ptr(); // device address of this device's status word (lazily set up)
 bool pdl_enabled();
 
