@@ -177,7 +177,10 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
 
 static int linear_common(LinearArgs& a, cudaStream_t stream) {
   if (a.M == 0) return NSQ_OK;
-  if (a.M <= kDecodeMaxM) return run_decode_linear(a, stream);
+  if (a.M <= kDecodeMaxM) {
+    const int rc = run_decode_linear(a, stream);
+    if (rc != NSQ_ENOTSUP) return rc;  // slice too large for the on-chip plan: tensor-core GEMM
+  }
   if (pair_prefill_supported(a)) return run_prefill_pair_linear(a, stream);
   return run_prefill_linear(a, stream);
 }
@@ -196,7 +199,6 @@ int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
   if (M == 0) return NSQ_OK;
   if (!x || !qweight || !scales || !zeros || !y) return NSQ_EINVAL;
   if (!aligned16(x) || !aligned16(y) || !aligned16(qweight)) return NSQ_EALIGN;
-  if (M <= kDecodeMaxM && K > 8 * 64 * 128) return NSQ_ENOTSUP;
   int rc = check_device();
   if (rc != NSQ_OK) return rc;
   LinearArgs a{};

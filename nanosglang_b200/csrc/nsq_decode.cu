@@ -8,11 +8,14 @@
 // Design (swap-AB skinny GEMM on the warp-level tensor path):
 //   * W rows (output features) form the MMA M dimension (16 per warp), tokens
 //     form MMA N (8 per n-tile), so M = 1..64 tokens costs 1..8 n-tiles.
-//   * CTA = 4 warps = 64 output rows x a K slice. Each warp streams its own
-//     16-row strip through a private ring of 1 KB TMA tiles taken straight
-//     from the reference layout (qweight [N, K/8] int32 or weight_fp8 [N, K]
-//     uint8); no repacked copy of the weight exists. All of a CTA's first
-//     tiles are requested before anything else happens.
+//   * CTA = 4 row groups of 16 rows (64 output rows) x a K slice, with 1-2
+//     warps per row group splitting that slice. The whole weight slice of each
+//     row group is requested at once as a few large TMA boxes (up to 16 rows x
+//     1 KB) straight from the reference layout (qweight [N, K/8] int32 or
+//     weight_fp8 [N, K] viewed as 32-bit words); no repacked copy of the
+//     weight exists. The issuing lane initialises its group's barriers itself,
+//     so the loads leave before anything else happens, and the next kernel on
+//     the stream is released (programmatic launch) right after.
 //   * x is copied with cp.async (all copies in flight at once, edges
 //     zero-filled) into an XOR-swizzled layout that makes every fragment load
 //     conflict-free.
@@ -39,10 +42,13 @@ namespace nsq {
 
 namespace {
 
-constexpr int kWarps = 4;
+constexpr int kRowWarps = 4;       // row groups of 16 rows per CTA
+constexpr int kMaxKGroups = 2;     // warps per row group splitting K (intra-CTA split-K)
+constexpr int kMaxThreads = kRowWarps * kMaxKGroups * 32;
 constexpr int kRows = 64;          // output rows per CTA
-constexpr int kNstMax = 8;         // TMA ring depth per warp (upper bound)
-constexpr int kStageBytes = 1024;  // 16 rows x 64 B
+constexpr int kMaxSlabs = 16;      // TMA boxes per row group (one barrier each)
+constexpr int kSlabRowMax = 1024;  // bytes per row of one TMA box (256 x 32-bit)
+constexpr int kWBudget = 96 * 1024;  // bytes of weight slice per CTA held in shared memory
 constexpr int kRedStride = 68;     // fp32 per token row of the partial tile (conflict-free)
 constexpr int kMaxSmem = 200 * 1024;
 constexpr int kXBudget = 48 * 1024;  // bytes for x staging buffers
@@ -72,11 +78,14 @@ struct DecodeParams {
   int group_size, G;
   int k_split;  // columns per CTA (multiple of the piece width)
   int pmax;     // pieces per CTA (k_split / piece)
-  int nst;      // TMA ring depth per warp
+  int kw;       // k-groups of warps inside the CTA (blockDim = 128 * kw)
+  int nslab;    // TMA boxes per row group
+  int slab_row; // bytes per row of one box (multiple of 64)
+  int pps;      // pieces per box
   int ppc;      // pieces per x staging chunk
   int xrs;      // bytes per token row of an x buffer (ppc * piece * 2)
   int bias_dtype;
-  int off_x, off_xsum, off_sz, off_red, off_bar, off_abort;
+  int off_x, off_xsum, off_sz, off_red, off_redk, off_bar, off_abort;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -110,7 +119,7 @@ __device__ __forceinline__ void issue_x_copy(const DecodeParams& p, uint32_t xbu
   const int cpr = np * F::kChunksPerPiece;  // 16-byte chunks per token row
   const int total = MPAD * cpr;
   const uint16_t* x = static_cast<const uint16_t*>(p.x);
-  for (int idx = tid; idx < total; idx += kWarps * 32) {
+  for (int idx = tid; idx < total; idx += blockDim.x) {
     const int t = idx / cpr;
     const int q = idx - t * cpr;
     const int k = kc0 + q * 8;
@@ -126,7 +135,7 @@ __device__ __forceinline__ void piece_sums(const DecodeParams& p, uint32_t xbuf,
                                            int tid) {
   constexpr int CPP = DecFmt<0>::kChunksPerPiece;
   const int total = np * MPAD * CPP;
-  for (int base = 0; base < total; base += kWarps * 32) {
+  for (int base = 0; base < total; base += blockDim.x) {
     const int item = base + tid;
     const bool valid = item < total;
     const int q = item % CPP;
@@ -260,12 +269,16 @@ __device__ __forceinline__ void fp8_piece(float (&acc)[MT][4], const uint4& wa, 
 }
 
 template <int FMT, bool BF16, int MT>
-__global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
+__global__ void __launch_bounds__(kMaxThreads, 2) decode_linear_kernel(
     const __grid_constant__ CUtensorMap wmap, const DecodeParams p) {
   using F = DecFmt<FMT>;
   constexpr int MPAD = MT * 8;
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nthreads = blockDim.x;
+  const int rg = warp & (kRowWarps - 1);  // which 16 of the 64 rows
+  const int kg = warp / kRowWarps;        // which k-group (pieces kg, kg+kw, ...)
+  const int kw = p.kw;
   const int g = lane >> 2, c = lane & 3;
   const int rank = blockIdx.x;  // split-K rank == rank in the cluster
   const int S = gridDim.x;
@@ -273,38 +286,35 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
   const int k_begin = rank * p.k_split;
   const int k_end = min(p.K, k_begin + p.k_split);
   const int P = (k_end - k_begin + F::kPieceK - 1) / F::kPieceK;
-  const int nst = p.nst;
+  const int nslab_used = (P + p.pps - 1) / p.pps;
+  const int group_bytes = 16 * p.slab_row * p.nslab;  // shared memory of one row group
 
-  const uint32_t wring = smem_u32(smem);
+  const uint32_t wgroup = smem_u32(smem) + rg * group_bytes;
   const uint32_t xbuf0 = smem_u32(smem + p.off_x);
   float* xsum = reinterpret_cast<float*>(smem + p.off_xsum);
   float* sz = reinterpret_cast<float*>(smem + p.off_sz);
   float* red = reinterpret_cast<float*>(smem + p.off_red);
-  uint64_t* bar_base = reinterpret_cast<uint64_t*>(smem + p.off_bar);
-  uint64_t* wbar = bar_base + warp * kNstMax;
+  float* redk = reinterpret_cast<float*>(smem + p.off_redk);
+  uint64_t* sbar = reinterpret_cast<uint64_t*>(smem + p.off_bar) + rg * kMaxSlabs;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.off_abort);
   const int xbuf_bytes = MPAD * p.xrs;
 
-  if (tid == 0) {
-    *abort_flag = 0;
-    for (int s = 0; s < kWarps * kNstMax; ++s) mbar_init(bar_base + s, 1);
-    fence_barrier_init();
+  // the first warp of each row group initialises that group's barriers and
+  // requests the group's whole weight slice before anything else
+  if (kg == 0 && lane == 0) {
+    for (int sl = 0; sl < nslab_used; ++sl) mbar_init(&sbar[sl], 1);
+    fence_proxy_async_smem();
+    const int kbytes = FMT == 0 ? k_begin / 2 : k_begin;  // byte offset of the slice in a row
+    for (int sl = 0; sl < nslab_used; ++sl) {
+      mbar_arrive_expect_tx(&sbar[sl], 16 * p.slab_row);
+      tma_load_2d(smem + rg * group_bytes + sl * 16 * p.slab_row, &wmap, &sbar[sl],
+                  (kbytes + sl * p.slab_row) / 4, n0 + 16 * rg);
+    }
   }
-  __syncthreads();
-
-  auto issue = [&](int j) {
-    const int buf = j % nst;
-    mbar_arrive_expect_tx(&wbar[buf], kStageBytes);
-    const int kk = k_begin + j * F::kPieceK;
-    tma_load_2d(smem + (warp * kNstMax + buf) * kStageBytes, &wmap, &wbar[buf],
-                FMT == 0 ? kk / 8 : kk, n0 + 16 * warp);
-  };
-  int issued = 0;
-  if (lane == 0) {
-    const int first = P < nst ? P : nst;
-    for (int j = 0; j < first; ++j) issue(j);
-    issued = first;
-  }
+  if (tid == 0) *abort_flag = 0;
+  // the next kernel on the stream may launch now and start its own weight
+  // loads; it still waits for this grid before it reads anything we write
+  pdl_launch_dependents();
 
   bool int_zeros = true;
   if constexpr (FMT == 0) {
@@ -313,11 +323,11 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
     constexpr float kZMax = BF16 ? 127.0f : 1023.0f;
     const int total = P * kRows;
     bool all_int = true;
-    for (int base = 0; base < total; base += kWarps * 32 * 8) {
+    for (int base = 0; base < total; base += nthreads * 8) {
       float sv[8], zv[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int idx = base + tid + kWarps * 32 * u;
+        const int idx = base + tid + nthreads * u;
         const int j = idx / kRows, r = idx % kRows;
         const int n = n0 + r;
         sv[u] = 0.f;
@@ -330,7 +340,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const int idx = base + tid + kWarps * 32 * u;
+        const int idx = base + tid + nthreads * u;
         if (idx < total) {
           const int j = idx / kRows, r = idx % kRows;
           sz[j * kRows + r] = sv[u];
@@ -339,20 +349,17 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
         }
       }
     }
-    int_zeros = __syncthreads_and(all_int ? 1 : 0) != 0;
+    int_zeros = all_int;  // combined across the CTA at the first barrier below
   }
 
-  // x (and bias) may be produced by the previous kernel on the stream; from
-  // here on the next kernel may start streaming its own weights
+  // x (and bias) may be produced by the previous kernel on the stream
   pdl_wait_prior_grids();
-  pdl_launch_dependents();
 
   float acc[MT][4];
 #pragma unroll
   for (int jt = 0; jt < MT; ++jt) acc[jt][0] = acc[jt][1] = acc[jt][2] = acc[jt][3] = 0.f;
 
   bool ok = true;
-  int consumed = 0;
   const int nchunks = (P + p.ppc - 1) / p.ppc;
   // x chunks double-buffered: the copy of chunk ch+1 flies while chunk ch computes
   issue_x_copy<FMT, MPAD>(p, xbuf0, k_begin, min(P, p.ppc), tid);
@@ -369,24 +376,31 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();  // chunk ch landed for every thread
+    if (ch == 0) {
+      // chunk 0 landed for every thread; scale/zero staging is visible and
+      // the integer-zero-point decision is made CTA-wide
+      int_zeros = __syncthreads_and(int_zeros ? 1 : 0) != 0;
+    } else {
+      __syncthreads();  // chunk ch landed for every thread
+    }
     if constexpr (FMT == 0) {
       if (!int_zeros) {
         piece_sums<BF16, MPAD>(p, xb, xsum, j1 - j0, tid);
         __syncthreads();
       }
     }
-    for (int j = j0; j < j1; ++j) {
-      const int buf = j % nst;
-      if (ok) ok = mbar_wait(&wbar[buf], (j / nst) & 1, p.status, 1, abort_flag);
+    // this warp's pieces in [j0, j1): j == kg (mod kw)
+    for (int j = j0 + ((kg - j0 % kw) + kw) % kw; j < j1; j += kw) {
+      const int sl = j / p.pps;
+      if (ok) ok = mbar_wait(&sbar[sl], 0, p.status, 1, abort_flag);
       if (ok) {
-        const uint32_t wt = wring + (warp * kNstMax + buf) * kStageBytes;
-        const uint4 wa = lds128(wt + g * 64 + c * 16);
-        const uint4 wb = lds128(wt + (g + 8) * 64 + c * 16);
+        const uint32_t wt = wgroup + sl * 16 * p.slab_row + (j - sl * p.pps) * 64;
+        const uint4 wa = lds128(wt + g * p.slab_row + c * 16);
+        const uint4 wb = lds128(wt + (g + 8) * p.slab_row + c * 16);
         const int jl = j - j0;
         const uint32_t xrow0 = xb + jl * F::kPieceK * 2;
         if constexpr (FMT == 0) {
-          const int r0 = 16 * warp + g;
+          const int r0 = 16 * rg + g;
           const float s0 = sz[j * kRows + r0], s1 = sz[j * kRows + r0 + 8];
           const float zb0 = sz[(p.pmax + j) * kRows + r0], zb1 = sz[(p.pmax + j) * kRows + r0 + 8];
           if (int_zeros) {
@@ -397,47 +411,76 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
         } else {
           fp8_piece<BF16, MT>(acc, wa, wb, xrow0, p.xrs, g, c);
         }
-        consumed = j + 1;
-      }
-      __syncwarp();
-      if (lane == 0 && ok && j + nst < P) {
-        issue(j + nst);
-        issued = j + nst + 1;
       }
     }
     if (ch + 1 < nchunks) __syncthreads();  // every warp is done with this x buffer
+  }
+
+  // k-groups 1.. hand their partial sums to k-group 0 through shared memory
+  if (kw > 1) {
+    if (kg > 0) {
+      float* dst = redk + (size_t)(kg - 1) * MPAD * kRedStride;
+#pragma unroll
+      for (int jt = 0; jt < MT; ++jt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = 8 * jt + 2 * c + (e & 1);
+          const int row = 16 * rg + g + 8 * (e >> 1);
+          dst[tok * kRedStride + row] = acc[jt][e];
+        }
+      }
+    }
+    __syncthreads();
+    if (kg == 0) {
+      for (int q = 1; q < kw; ++q) {
+        const float* src = redk + (size_t)(q - 1) * MPAD * kRedStride;
+#pragma unroll
+        for (int jt = 0; jt < MT; ++jt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int tok = 8 * jt + 2 * c + (e & 1);
+            const int row = 16 * rg + g + 8 * (e >> 1);
+            acc[jt][e] += src[tok * kRedStride + row];
+          }
+        }
+      }
+    }
   }
 
   const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
   uint16_t* y = static_cast<uint16_t*>(p.y);
   if (S == 1) {
     // unsplit: scale, bias and store straight from the accumulators
-    const int ra = n0 + 16 * warp + g, rb = ra + 8;
-    float ba = 0.f, bb = 0.f;
-    if (p.bias_dtype != NSQ_DTYPE_NONE) {
-      if (ra < p.N) ba = load_bias(p.bias, p.bias_dtype, ra);
-      if (rb < p.N) bb = load_bias(p.bias, p.bias_dtype, rb);
-    }
+    if (kg == 0) {
+      const int ra = n0 + 16 * rg + g, rb = ra + 8;
+      float ba = 0.f, bb = 0.f;
+      if (p.bias_dtype != NSQ_DTYPE_NONE) {
+        if (ra < p.N) ba = load_bias(p.bias, p.bias_dtype, ra);
+        if (rb < p.N) bb = load_bias(p.bias, p.bias_dtype, rb);
+      }
 #pragma unroll
-    for (int jt = 0; jt < MT; ++jt) {
+      for (int jt = 0; jt < MT; ++jt) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tok = 8 * jt + 2 * c + (e & 1);
-        const int n = (e >> 1) ? rb : ra;
-        if (tok < p.M && n < p.N) {
-          y[(int64_t)tok * p.N + n] = float_to_elem<BF16>(fmaf(acc[jt][e], wscale, (e >> 1) ? bb : ba));
+        for (int e = 0; e < 4; ++e) {
+          const int tok = 8 * jt + 2 * c + (e & 1);
+          const int n = (e >> 1) ? rb : ra;
+          if (tok < p.M && n < p.N) {
+            y[(int64_t)tok * p.N + n] = float_to_elem<BF16>(fmaf(acc[jt][e], wscale, (e >> 1) ? bb : ba));
+          }
         }
       }
     }
   } else {
     // partial tile -> shared memory [token][row], reduced across the cluster
+    if (kg == 0) {
 #pragma unroll
-    for (int jt = 0; jt < MT; ++jt) {
+      for (int jt = 0; jt < MT; ++jt) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tok = 8 * jt + 2 * c + (e & 1);
-        const int row = 16 * warp + g + 8 * (e >> 1);
-        red[tok * kRedStride + row] = acc[jt][e];
+        for (int e = 0; e < 4; ++e) {
+          const int tok = 8 * jt + 2 * c + (e & 1);
+          const int row = 16 * rg + g + 8 * (e >> 1);
+          red[tok * kRedStride + row] = acc[jt][e];
+        }
       }
     }
     cluster_sync_all();
@@ -445,7 +488,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
     const int per = (E + S - 1) / S;
     const int e0 = rank * per;
     const int e1 = min(E, e0 + per);
-    for (int e = e0 + tid; e < e1; e += kWarps * 32) {
+    for (int e = e0 + tid; e < e1; e += nthreads) {
       const int tok = e / kRows, row = e % kRows;
       const int n = n0 + row;
       if (n >= p.N) continue;
@@ -459,40 +502,53 @@ __global__ void __launch_bounds__(kWarps * 32) decode_linear_kernel(
     cluster_sync_all();
   }
 
-  // after an abort, let this warp's outstanding copies land before exiting
-  if (lane == 0 && !ok) {
-    for (int j = consumed; j < issued; ++j) {
-      mbar_wait(&wbar[j % nst], (j / nst) & 1, nullptr, 0, nullptr);
-    }
+  // after an abort, let this group's copies land before the CTA exits
+  if (!ok && kg == 0 && lane == 0) {
+    for (int sl = 0; sl < nslab_used; ++sl) mbar_wait(&sbar[sl], 0, nullptr, 0, nullptr);
   }
 }
 
 struct Plan {
-  int S, k_split, pmax, nst, ppc, xrs;
+  bool ok;
+  int S, k_split, pmax, kw, nslab, slab_row, pps, ppc, xrs;
   size_t smem;
-  int off_x, off_xsum, off_sz, off_red, off_bar, off_abort;
+  int off_x, off_xsum, off_sz, off_red, off_redk, off_bar, off_abort;
 };
 
 template <int FMT>
 Plan make_plan(int M, int K, int N) {
   using F = DecFmt<FMT>;
+  constexpr int kPieceRowBytes = 64;  // one piece of one weight row in shared memory
   Plan pl{};
   const int mpad = ((M + 7) / 8) * 8;
   const int pieces = (K + F::kPieceK - 1) / F::kPieceK;
   const int rt = (N + kRows - 1) / kRows;
   const int sms = num_sms();
-  // split K only as far as needed to put a CTA on every SM
+  // split K across the CTAs of a cluster only as far as needed to put a CTA
+  // on every SM, and far enough that a CTA's weight slice fits on chip
   int S = (sms + rt - 1) / rt;
   S = S < 1 ? 1 : S;
-  S = S > 8 ? 8 : S;
+  const int min_s = (int)(((size_t)pieces * kPieceRowBytes * kRows + kWBudget - 1) / kWBudget);
+  S = S < min_s ? min_s : S;
+  S = S > 8 ? 8 : S;  // portable cluster size
   S = S > pieces ? pieces : S;
   int per = (pieces + S - 1) / S;
-  if (FMT == 0 && per > 64) per = 64;  // bounded scale/zero staging
   S = (pieces + per - 1) / per;
+  pl.ok = (size_t)per * kPieceRowBytes * kRows <= (size_t)kWBudget && (FMT != 0 || per <= 64);
   pl.S = S;
   pl.pmax = per;
   pl.k_split = per * F::kPieceK;
-  pl.nst = per < kNstMax ? per : kNstMax;
+  // boxes of equal width covering the slice with little overhang
+  const int row_bytes = per * kPieceRowBytes;
+  int nslab = (row_bytes + kSlabRowMax - 1) / kSlabRowMax;
+  int slab_pieces = (per + nslab - 1) / nslab;
+  nslab = (per + slab_pieces - 1) / slab_pieces;
+  pl.pps = slab_pieces;
+  pl.slab_row = slab_pieces * kPieceRowBytes;
+  pl.nslab = nslab;
+  if (nslab > kMaxSlabs) pl.ok = false;
+  // two warps per row group when each can keep at least two pieces
+  pl.kw = per >= 4 ? 2 : 1;
   // x staging: one buffer for the whole slice if it fits, else two chunk buffers
   const int piece_token_bytes = F::kPieceK * 2;
   int nbuf;
@@ -505,7 +561,8 @@ Plan make_plan(int M, int K, int N) {
     nbuf = 2;
   }
   pl.xrs = pl.ppc * piece_token_bytes;
-  size_t off = (size_t)kWarps * kNstMax * kStageBytes;
+  size_t off = (size_t)kRowWarps * 16 * pl.slab_row * pl.nslab;
+  off = (off + 127) & ~(size_t)127;
   pl.off_x = (int)off;
   off += (size_t)nbuf * mpad * pl.xrs;
   pl.off_xsum = (int)off;
@@ -515,12 +572,15 @@ Plan make_plan(int M, int K, int N) {
   off = (off + 15) & ~(size_t)15;
   pl.off_red = (int)off;
   off += (S > 1) ? (size_t)mpad * kRedStride * 4 : 0;
+  pl.off_redk = (int)off;
+  off += (size_t)(pl.kw - 1) * mpad * kRedStride * 4;
   off = (off + 7) & ~(size_t)7;
   pl.off_bar = (int)off;
-  off += (size_t)kWarps * kNstMax * 8;
+  off += (size_t)kRowWarps * kMaxSlabs * 8;
   pl.off_abort = (int)off;
   off += 16;
   pl.smem = off;
+  if (pl.smem > (size_t)kMaxSmem) pl.ok = false;
   return pl;
 }
 
@@ -540,7 +600,7 @@ cudaError_t launch_t(const CUtensorMap& map, const DecodeParams& p, const Plan& 
   if (pl.smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.S, (p.N + kRows - 1) / kRows, 1);
-  cfg.blockDim = dim3(kWarps * 32, 1, 1);
+  cfg.blockDim = dim3(kRowWarps * pl.kw * 32, 1, 1);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
@@ -582,19 +642,14 @@ cudaError_t dispatch_mt(int mt, const CUtensorMap& map, const DecodeParams& p, c
 int run_decode_linear(const LinearArgs& a, cudaStream_t stream) {
   const int mt = (a.M + 7) / 8;
   Plan pl = a.fmt == 0 ? make_plan<0>(a.M, a.K, a.N) : make_plan<1>(a.M, a.K, a.N);
+  if (!pl.ok) return NSQ_ENOTSUP;
+  // both formats viewed as rows of 32-bit words: qweight [N, K/8] int32,
+  // weight_fp8 [N, K] as [N, K/4]; one box = slab_row bytes x 16 rows
   CUtensorMap map;
-  CUresult cr;
-  if (a.fmt == 0) {
-    // qweight [N, K/8] int32: box = 16 words (128 columns) x 16 rows
-    cr = encode_tensor_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<void*>(a.wq),
-                              (uint64_t)a.K / 8, (uint64_t)a.N, (uint64_t)a.K / 2, 16, 16,
-                              CU_TENSOR_MAP_SWIZZLE_NONE);
-  } else {
-    // weight_fp8 [N, K] uint8: box = 64 columns x 16 rows
-    cr = encode_tensor_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<void*>(a.wq),
-                              (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, 64, 16,
-                              CU_TENSOR_MAP_SWIZZLE_NONE);
-  }
+  const uint64_t row_bytes = a.fmt == 0 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
+  CUresult cr = encode_tensor_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<void*>(a.wq),
+                                     row_bytes / 4, (uint64_t)a.N, row_bytes, pl.slab_row / 4, 16,
+                                     CU_TENSOR_MAP_SWIZZLE_NONE);
   if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
   DecodeParams p{};
   p.x = a.x;
@@ -611,7 +666,10 @@ int run_decode_linear(const LinearArgs& a, cudaStream_t stream) {
   p.G = a.fmt == 0 ? (a.K + a.group_size - 1) / a.group_size : 0;
   p.k_split = pl.k_split;
   p.pmax = pl.pmax;
-  p.nst = pl.nst;
+  p.kw = pl.kw;
+  p.nslab = pl.nslab;
+  p.slab_row = pl.slab_row;
+  p.pps = pl.pps;
   p.ppc = pl.ppc;
   p.xrs = pl.xrs;
   p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
@@ -619,6 +677,7 @@ int run_decode_linear(const LinearArgs& a, cudaStream_t stream) {
   p.off_xsum = pl.off_xsum;
   p.off_sz = pl.off_sz;
   p.off_red = pl.off_red;
+  p.off_redk = pl.off_redk;
   p.off_bar = pl.off_bar;
   p.off_abort = pl.off_abort;
   cudaError_t e;
