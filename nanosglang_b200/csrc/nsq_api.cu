@@ -178,8 +178,27 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
 static int linear_common(LinearArgs& a, cudaStream_t stream) {
   if (a.M == 0) return NSQ_OK;
   if (a.M <= kDecodeMaxM) {
-    const int rc = run_decode_linear(a, stream);
-    if (rc != NSQ_ENOTSUP) return rc;  // slice too large for the on-chip plan: tensor-core GEMM
+    // Three decode kernels, chosen by shape (measured in CUDA-graph chains of
+    // distinct weights on B200):
+    //   * layers whose multi-wave plan needs more than two CTAs per SM: the
+    //     persistent weight-ring kernel (up to 32 tokens);
+    //   * short K (one 1 KB slice per row) with few tokens or few rows: the
+    //     single-wave kernel;
+    //   * otherwise the multi-wave kernel; the tensor-core GEMM when no
+    //     decode plan fits.
+    const int ctas = decode_linear_ctas(a);
+    if (ctas < 0 || ctas > 2 * num_sms()) {
+      const int rc = run_decode_stream_linear(a, stream);
+      if (rc != NSQ_ENOTSUP) return rc;
+    }
+    if (a.K <= 1024 && (a.M <= 8 || a.N <= 1024)) {
+      const int rc = run_decode_wave_linear(a, stream);
+      if (rc != NSQ_ENOTSUP) return rc;
+    }
+    int rc = run_decode_linear(a, stream);
+    if (rc != NSQ_ENOTSUP) return rc;
+    rc = run_decode_wave_linear(a, stream);
+    if (rc != NSQ_ENOTSUP) return rc;
   }
   if (pair_prefill_supported(a)) return run_prefill_pair_linear(a, stream);
   return run_prefill_linear(a, stream);

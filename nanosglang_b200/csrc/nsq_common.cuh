@@ -432,6 +432,24 @@ __device__ __forceinline__ void unpack_nibble_pairs(uint32_t w, uint32_t (&e)[4]
   e[3] = lop3_and_or(w >> 12, 0x000F000Fu, M);
 }
 
+// The A operands of the two m16n8k16 MMAs of one word of row g (wg) and the
+// same word of row g + 8 (wh), written straight in fragment order:
+//   a0 = {p0(wg), p0(wh), p1(wg), p1(wh)},  a1 = {p2(wg), p2(wh), p3(wg), p3(wh)}
+// with p_t = {magic+q_t, magic+q_{t+4}} as in unpack_nibble_pairs.
+template <bool BF16>
+__device__ __forceinline__ void nibble_quads(uint32_t wg, uint32_t wh, uint32_t (&a0)[4],
+                                             uint32_t (&a1)[4]) {
+  constexpr uint32_t M = Magic<BF16>::kPair;
+  a0[0] = lop3_and_or(wg, 0x000F000Fu, M);
+  a0[1] = lop3_and_or(wh, 0x000F000Fu, M);
+  a0[2] = lop3_and_or(wg >> 4, 0x000F000Fu, M);
+  a0[3] = lop3_and_or(wh >> 4, 0x000F000Fu, M);
+  a1[0] = lop3_and_or(wg >> 8, 0x000F000Fu, M);
+  a1[1] = lop3_and_or(wh >> 8, 0x000F000Fu, M);
+  a1[2] = lop3_and_or(wg >> 12, 0x000F000Fu, M);
+  a1[3] = lop3_and_or(wh >> 12, 0x000F000Fu, M);
+}
+
 // Four e4m3 codes (one word, low byte first) -> two packed pairs of the MMA
 // element type, exact, with integer ops plus one packed multiply per pair
 // (no conversion-pipe instructions). The sign bit goes to bit 15 and the
@@ -496,6 +514,22 @@ __device__ __forceinline__ float load_bias(const void* bias, int dtype, int n) {
     default:
       return 0.0f;
   }
+}
+
+// n / d for 0 <= n < 2^31 with one multiply-high, one add and one shift: the
+// invariant-divisor method of Granlund & Montgomery (PLDI 1994) with the
+// 33-bit multiplier 2^32 + mul, l = ceil(log2 d), mul = floor(2^32 (2^l - d) / d) + 1.
+struct FastDiv {
+  uint32_t mul, shift;
+};
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while (l < 31 && (1u << l) < d) ++l;
+  const uint64_t m = ((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1;
+  return FastDiv{static_cast<uint32_t>(m), l};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, FastDiv f) {
+  return (__umulhi(n, f.mul) + n) >> f.shift;
 }
 
 }  // namespace nsq

@@ -639,6 +639,11 @@ cudaError_t dispatch_mt(int mt, const CUtensorMap& map, const DecodeParams& p, c
 
 }  // namespace
 
+int decode_linear_ctas(const LinearArgs& a) {
+  const Plan pl = a.fmt == 0 ? make_plan<0>(a.M, a.K, a.N) : make_plan<1>(a.M, a.K, a.N);
+  return pl.ok ? pl.S * ((a.N + kRows - 1) / kRows) : -1;
+}
+
 int run_decode_linear(const LinearArgs& a, cudaStream_t stream) {
   const int mt = (a.M + 7) / 8;
   Plan pl = a.fmt == 0 ? make_plan<0>(a.M, a.K, a.N) : make_plan<1>(a.M, a.K, a.N);

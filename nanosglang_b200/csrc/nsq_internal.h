@@ -48,7 +48,10 @@ struct LinearArgs {
   int bias_dtype;
   void* y;
 };
-int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64
+int run_decode_wave_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 64, one wave of CTAs
+int run_decode_stream_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 64, persistent weight ring
+int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64, one or more waves
+int decode_linear_ctas(const LinearArgs& a);  // CTAs run_decode_linear launches, -1 if it cannot
 int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M, one CTA per tile
 bool pair_prefill_supported(const LinearArgs& a);
 int run_prefill_pair_linear(const LinearArgs& a, cudaStream_t stream);  // M > 128, CTA pairs

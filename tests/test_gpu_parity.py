@@ -188,6 +188,14 @@ def test_awq_linear_decode_shapes(n, k, gs, zm, bias, m):
     assert err <= GEMM_TOL, err
 
 
+@pytest.mark.parametrize("m", [1, 16, 24, 32])
+def test_awq_linear_decode_large_layer(m):
+    """Llama-3-8B gate shape: large enough for the streamed weight-ring kernel."""
+    err = _awq_case(m, 14336, 4096, 128, torch.bfloat16, bias=(m == 1), zm="frac" if m == 24 else "int",
+                    seed=500 + m)
+    assert err <= GEMM_TOL, err
+
+
 @pytest.mark.parametrize("m", [65, 128, 200, 1024])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_awq_linear_prefill(m, dtype):
@@ -253,6 +261,12 @@ def test_fp8_linear_config1(kn, m):
     k, n = kn
     err = _fp8_case(m, n, k, torch.bfloat16, bias=(n == 128), seed=m * 7 + n)
     assert err <= GEMM_TOL, err
+
+
+@pytest.mark.parametrize("m", [1, 8, 32])
+def test_fp8_linear_decode_large_layer(m):
+    assert _fp8_case(m, 14336, 4096, torch.bfloat16, bias=(m == 8), seed=700 + m) <= GEMM_TOL
+    assert _fp8_case(m, 4096, 14336, torch.float16, bias=False, seed=800 + m) <= GEMM_TOL
 
 
 @pytest.mark.parametrize("m", [5, 64, 300])
