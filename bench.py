@@ -25,6 +25,12 @@ absmax/448 scale, bf16 N(0,1) activations. Random init, synthetic data.
 --gpus N (under torchrun): tensor parallel over the same sweep, q/k/v/gate/up
 column-parallel, o/down row-parallel + NCCL all_reduce; max-over-ranks time.
 --impl reference: the CPU oracle alone on the same workload (rank 0 only).
+--ncu-case NAME: run a few launches of one kernel class and exit (no timing,
+no JSON), for Nsight Compute captures of a small case:
+  prefill        FP8 gate shape, M=16384 (tcgen05 paired-CTA GEMM), 3 launches
+  sweep_prefill  the sweep's M > 64 linears once each (the roofline kernel's launches)
+  decode         the sweep's M <= 64 linears once each
+  awq0           config-0 AWQ linear (M=16, K=896, N=9728), 4 launches
 """
 
 from __future__ import annotations
@@ -347,7 +353,7 @@ def run_ours(args):
     ms_dec = time_graph(g_dec, args.steps, args.warmup)
     bytes_dec = sum(case_bytes_flops(c["m"], c["ks"], c["ns"])[0] for c in dec)
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-    decode_line = {"kernel": "decode_linear_kernel<FP8,bf16> (mma.sync swap-AB, split-K over clusters)",
+    decode_line = {"kernel": "decode kernels (mma.sync swap-AB: single-wave / multi-wave / weight ring, by shape)",
                    "bound": "hbm", "achieved": round(bytes_dec / (ms_dec * 1e-3) / 1e9, 1),
                    "peak": hbm_peak, "unit": "GB/s",
                    "frac": round(bytes_dec / (ms_dec * 1e-3) / 1e9 / hbm_peak, 4),
@@ -491,6 +497,43 @@ def run_reference(args):
         "e2e": {"value": round(r["value"], 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_ncu_case(name):
+    """A handful of launches of one kernel class, for an Nsight Compute capture."""
+    import torch
+
+    from nanosglang_b200 import _lib, ops
+    _lib.load()
+    _lib.set_pdl(True)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(0)
+    if name == "prefill":
+        m, k, n = 16384, 896, 4864
+        codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        for _ in range(3):
+            ops.fp8_linear(x, codes, scale)
+    elif name in ("decode", "sweep_prefill"):
+        for _, k, n in SHAPES:
+            codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
+            for m in [mm for mm in MS if (mm <= 64) == (name == "decode")]:
+                x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+                ops.fp8_linear(x, codes, scale)
+    elif name == "awq0":
+        m, k, n, gs = 16, 896, 9728, 128
+        for _ in range(4):
+            qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), generator=g, dtype=torch.int64).to(torch.int32)
+            s = (torch.rand(n, k // gs, generator=g) * 0.009 + 0.001).half()
+            z = torch.randint(0, 16, (n, k // gs), generator=g).half()
+            x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+            ops.awq_linear(x.to(dev), qw.to(dev), s.to(dev), z.to(dev), gs)
+    else:
+        raise SystemExit(f"unknown --ncu-case {name}")
+    torch.cuda.synchronize()
+    code, where, block = _lib.device_status()
+    if code != 0:
+        raise RuntimeError(f"device status {code} (tag {where}, block {block})")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -499,7 +542,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle leg")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--ncu-case", choices=["prefill", "sweep_prefill", "decode", "awq0"], default=None,
+                    help="run a small case of one kernel class for a profiler capture, then exit")
     args = ap.parse_args()
+    if args.ncu_case:
+        run_ncu_case(args.ncu_case)
+        return
     args.warmup = max(3, args.warmup)
     out = run_reference(args) if args.impl == "reference" else run_ours(args)
     if out is not None:

@@ -365,6 +365,22 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
 }
+// Cluster barrier halves (not .aligned: callable where the warp diverged).
+__device__ __forceinline__ void cluster_arrive_rel() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acq() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+// 16-byte store into another CTA's shared memory, counted on its barrier.
+__device__ __forceinline__ void st_async_f32x4(uint32_t cluster_addr, float a, float b, float c, float d,
+                                               uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          cluster_addr),
+      "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
+      : "memory");
+}
 __device__ __forceinline__ uint32_t dsmem_map(uint32_t smem_addr, uint32_t cta_rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(cta_rank));

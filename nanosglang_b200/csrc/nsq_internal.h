@@ -52,7 +52,8 @@ int run_decode_wave_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 6
 int run_decode_stream_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 64, persistent weight ring
 int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64, one or more waves
 int decode_linear_ctas(const LinearArgs& a);  // CTAs run_decode_linear launches, -1 if it cannot
-int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M, one CTA per tile
+int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M, one CTA per tile (K split over a cluster when few tiles)
+int prefill_split_factor(int64_t M, int64_t K, int64_t N);      // CTAs per tile along K (1: no split)
 bool pair_prefill_supported(const LinearArgs& a);
 int run_prefill_pair_linear(const LinearArgs& a, cudaStream_t stream);  // M > 128, CTA pairs
 
