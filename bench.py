@@ -69,6 +69,23 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "traffic_config1_sweep_launches.txt")
+
+
+def profiled_traffic(case):
+    """Mean DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum) of the
+    sweep's prefill or decode launches, from the committed capture summary; None if absent."""
+    try:
+        with open(TRAFFIC_PROFILE) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == case:
+                    return int(float(parts[2]))
+    except OSError:
+        pass
+    return None
+
+
 def case_bytes_flops(m, k, n, fmt="fp8", gs=128):
     if fmt == "fp8":
         b = n * k + 4 + 2 * m * k + 2 * m * n
@@ -343,10 +360,14 @@ def run_ours(args):
     flops_pre = sum(2 * c["m"] * c["ns"] * c["ks"] for c in pre_k)
     bf16_peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     ach = flops_pre / (ms_pre * 1e-3) / 1e12
-    roofline = {"kernel": "prefill_linear_kernel<FP8,bf16> (tcgen05 kind::f16, TMEM accumulators)",
+    roofline = {"kernel": "prefill GEMMs (tcgen05 kind::f16, TMEM accumulators: paired-CTA, one-CTA, split-K cluster)",
                 "bound": "tensor", "achieved": round(ach, 2), "peak": bf16_peak, "unit": "TFLOP/s",
                 "frac": round(ach / bf16_peak, 4), "peak_source": f"{peak_src} bf16 dense (burst)",
-                "launches_per_step": len(pre_k), "traffic": None}
+                "launches_per_step": len(pre_k),
+                "traffic": profiled_traffic("sweep_prefill") if world == 1 else None,
+                "algorithmic_bytes_per_launch": int(sum(case_bytes_flops(c["m"], c["ks"], c["ns"])[0]
+                                                        for c in pre_k) / len(pre_k)),
+                "traffic_source": "ncu capture, mean per launch of the same 21 linears"}
     # decode kernel (M <= 64) class, for context
     dec = [dict(c, row=False) for c in cases if c["m"] <= 64]
     g_dec = capture(dec)
@@ -357,7 +378,9 @@ def run_ours(args):
                    "bound": "hbm", "achieved": round(bytes_dec / (ms_dec * 1e-3) / 1e9, 1),
                    "peak": hbm_peak, "unit": "GB/s",
                    "frac": round(bytes_dec / (ms_dec * 1e-3) / 1e9 / hbm_peak, 4),
-                   "launches_per_step": len(dec), "us_per_launch": round(ms_dec * 1e3 / len(dec), 2)}
+                   "launches_per_step": len(dec), "us_per_launch": round(ms_dec * 1e3 / len(dec), 2),
+                   "traffic": profiled_traffic("decode") if world == 1 else None,
+                   "algorithmic_bytes_per_launch": int(bytes_dec / len(dec))}
     del g_all, g_pre, g_dec
 
     # --- e2e through the module API with host buffers -----------------------
