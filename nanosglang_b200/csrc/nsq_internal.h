@@ -56,6 +56,10 @@ int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M, one
 int prefill_split_factor(int64_t M, int64_t K, int64_t N);      // CTAs per tile along K (1: no split)
 bool pair_prefill_supported(const LinearArgs& a);
 int run_prefill_pair_linear(const LinearArgs& a, cudaStream_t stream);  // M > 128, CTA pairs
+// weight tile dequantised into tensor memory (A operand), tokens as UMMA N;
+// tokens_per_tile 64, 128 or 192
+int run_prefill_ts_linear(const LinearArgs& a, int tokens_per_tile, cudaStream_t stream);
+int prefill_ts_tokens_per_tile(int64_t M, int64_t K, int64_t N);  // 0: use the other prefill kernels
 
 constexpr int kDecodeMaxM = 64;
 

@@ -209,6 +209,19 @@ def test_awq_linear_prefill_shapes(n, k, gs, zm):
     assert err <= GEMM_TOL, err
 
 
+@pytest.mark.parametrize("m,n,k,gs,zm", [(77, 131, 1024, 128, "frac"), (200, 896, 896, 128, "int"),
+                                         (1000, 896, 896, 256, "wide"), (8192, 128, 896, 128, "int"),
+                                         (300, 300, 608, 128, "frac")])
+def test_awq_linear_small_output_shapes(m, n, k, gs, zm):
+    """Prefill problems with at most 2^20 outputs (the TMEM-operand kernel):
+    groups spanning 2 or 4 k-blocks, a partial last group, non-integer and
+    out-of-range zero points."""
+    err = _awq_case(m, n, k, gs, torch.bfloat16, bias=True, zm=zm, seed=m * 3 + n)
+    assert err <= GEMM_TOL, err
+    err = _awq_case(m, n, k, gs, torch.float16, bias=False, zm=zm, seed=m * 3 + n + 1)
+    assert err <= GEMM_TOL, err
+
+
 def test_awq_linear_fp16_matches_reference_forward_golden():
     """The reference's own fp16 forward outputs (cases the kernels support)."""
     from nanosglang_b200 import ops
@@ -273,6 +286,15 @@ def test_fp8_linear_decode_large_layer(m):
 def test_fp8_linear_fp16_and_odd_shapes(m):
     assert _fp8_case(m, 200, 112, torch.float16, bias=True, seed=m) <= GEMM_TOL
     assert _fp8_case(m, 520, 608, torch.bfloat16, bias=False, seed=m + 1) <= GEMM_TOL
+
+
+@pytest.mark.parametrize("m,n,k", [(77, 130, 896), (200, 896, 512), (1000, 896, 896), (8192, 128, 896),
+                                   (129, 4864, 896), (300, 520, 608)])
+def test_fp8_linear_small_output_shapes(m, n, k):
+    """Prefill problems with at most 2^20 outputs (the TMEM-operand kernel):
+    ragged token tiles, odd N, a partial last k-block, bias, fp16."""
+    assert _fp8_case(m, n, k, torch.bfloat16, bias=(m % 2 == 1), seed=m + n) <= GEMM_TOL
+    assert _fp8_case(m, n, k, torch.float16, bias=(m % 2 == 0), seed=m + n + 1) <= GEMM_TOL
 
 
 def test_fp8_linear_vs_reference_forward_golden():
