@@ -360,7 +360,7 @@ def run_ours(args):
     flops_pre = sum(2 * c["m"] * c["ns"] * c["ks"] for c in pre_k)
     bf16_peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     ach = flops_pre / (ms_pre * 1e-3) / 1e12
-    roofline = {"kernel": "prefill GEMMs (tcgen05 kind::f16, TMEM accumulators: paired-CTA, one-CTA, split-K cluster)",
+    roofline = {"kernel": "prefill GEMMs (tcgen05 kind::f16; dequantised weight as the TMEM operand: paired-CTA and one-CTA; split-K cluster)",
                 "bound": "tensor", "achieved": round(ach, 2), "peak": bf16_peak, "unit": "TFLOP/s",
                 "frac": round(ach / bf16_peak, 4), "peak_source": f"{peak_src} bf16 dense (burst)",
                 "launches_per_step": len(pre_k),

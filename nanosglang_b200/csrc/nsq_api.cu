@@ -201,13 +201,13 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     if (rc != NSQ_ENOTSUP) return rc;
   }
   // Prefill: the one-CTA GEMM with K split over a thread-block cluster when
-  // its 128 x 256 tiles leave most SMs idle and K is long; the TMEM-operand
-  // GEMM for small outputs; the paired-CTA GEMM for problems that fill the
-  // GPU with 256 x 256 tiles; the one-CTA GEMM for the rest.
+  // its 128 x 256 tiles leave most SMs idle and K is long; else the weight
+  // tile dequantised into tensor memory -- one CTA per 128 rows for small
+  // outputs, CTA pairs (256 rows x 256 tokens) for the rest.
   if (prefill_split_factor(a.M, a.K, a.N) == 1) {
     const int bt = prefill_ts_tokens_per_tile(a.M, a.K, a.N);
     if (bt > 0) return run_prefill_ts_linear(a, bt, stream);
-    if (pair_prefill_supported(a)) return run_prefill_pair_linear(a, stream);
+    return run_prefill_ts2_linear(a, stream);
   }
   return run_prefill_linear(a, stream);
 }

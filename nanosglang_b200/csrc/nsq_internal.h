@@ -54,12 +54,13 @@ int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64, o
 int decode_linear_ctas(const LinearArgs& a);  // CTAs run_decode_linear launches, -1 if it cannot
 int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M, one CTA per tile (K split over a cluster when few tiles)
 int prefill_split_factor(int64_t M, int64_t K, int64_t N);      // CTAs per tile along K (1: no split)
-bool pair_prefill_supported(const LinearArgs& a);
-int run_prefill_pair_linear(const LinearArgs& a, cudaStream_t stream);  // M > 128, CTA pairs
 // weight tile dequantised into tensor memory (A operand), tokens as UMMA N;
 // tokens_per_tile 64, 128 or 192
 int run_prefill_ts_linear(const LinearArgs& a, int tokens_per_tile, cudaStream_t stream);
 int prefill_ts_tokens_per_tile(int64_t M, int64_t K, int64_t N);  // 0: use the other prefill kernels
+// CTA pairs, weight tile dequantised into each CTA's tensor memory, 256 weight
+// rows x 256 tokens per pair tile
+int run_prefill_ts2_linear(const LinearArgs& a, cudaStream_t stream);
 
 constexpr int kDecodeMaxM = 64;
 

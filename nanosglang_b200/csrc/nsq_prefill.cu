@@ -9,17 +9,19 @@
 // tile at a time per CTA, fp32 accumulators in tensor memory:
 //   warp 0        TMA producer: x tile [128 x 64] (128-byte swizzle) and the
 //                 packed weight tile [256 rows x 64 columns] of the reference
-//                 layout into a 4-stage ring.
+//                 layout into an NS-stage ring (shared with the converted tiles).
 //   warp 1        tcgen05.mma issuer (one thread), 128x256x16 kind::f16 steps;
 //                 also owns the 512-column TMEM allocation (2 accumulators).
 //   warps 2..9    converters: one weight row per thread; unpack int4 (AWQ,
 //                 zero point and group scale applied) or e4m3 (FP8) into the
 //                 MMA element type, written in the UMMA 128-byte-swizzled
-//                 K-major layout into a 2-stage ring.
+//                 K-major layout.
 //   warps 10..13  epilogue: tcgen05.ld of the finished accumulator, per-tensor
 //                 scale (FP8), bias, rounding to the activation dtype, store.
 // The accumulator is double-buffered so the epilogue of tile i overlaps the
-// main loop of tile i+1. Every mbarrier wait is bounded.
+// main loop of tile i+1. The UMMA issuer waits on one barrier and commits one
+// per k-block (each barrier operation in its loop delays the next UMMA).
+// Every mbarrier wait is bounded.
 //
 // Split-K (problems whose tiles leave most SMs idle, e.g. M = 128): the K
 // range of a tile is split over the `ksplit` CTAs of a thread-block cluster
@@ -41,8 +43,7 @@ namespace {
 constexpr int BM = 128;  // tokens per tile (UMMA M, TMEM lanes)
 constexpr int BN = 256;  // output features per tile (UMMA N, TMEM columns)
 constexpr int BK = 64;   // columns per k-block (one 128-byte swizzle row of 16-bit)
-constexpr int NL = 4;    // load stages
-constexpr int NB = 2;    // converted-weight stages
+constexpr int NS = 3;    // stages (x tile, packed weight tile, converted weight tile)
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpConv0 = 2;
@@ -84,16 +85,19 @@ struct PrefillParams {
 template <int FMT>
 struct Smem {
   static constexpr int kX = 0;
-  static constexpr int kB = kX + NL * kXTileBytes;
-  static constexpr int kWc = kB + NB * kBTileBytes;
-  static constexpr int kBar = kWc + NL * PreFmt<FMT>::kWcBytes;
-  // barriers: full_l[NL], empty_l[NL], full_b[NB], empty_b[NB], full_acc[2], empty_acc[2]
-  static constexpr int kNumBars = 2 * NL + 2 * NB + 4;
+  static constexpr int kB = kX + NS * kXTileBytes;
+  static constexpr int kWc = kB + NS * kBTileBytes;
+  static constexpr int kBar = kWc + NS * PreFmt<FMT>::kWcBytes;
+  // barriers: full_l[NS], read_w[NS], full_b[NS], mma_done[NS], full_acc[2], empty_acc[2]
+  static constexpr int kNumBars = 4 * NS + 4;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kRecvBar = kAbort + 4;  // split-K: partial tiles received (8-byte aligned)
   static constexpr int kTotal = kRecvBar + 8;
   static constexpr int kAlloc = kTotal + 1024;  // room to align the base to 1 KB
+  static_assert(kAlloc <= 227 * 1024, "shared memory per CTA");
+  // split-K receives up to 128 KB of partial tiles at kX (x and B rings)
+  static_assert(kWc - kX >= 128 * 1024, "split-K receive slots");
 };
 
 // Per-row dequant parameters for one AWQ group, in the MMA element type.
@@ -214,11 +218,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  // Per stage s: full_l (TMA bytes of x and the packed weight), read_w (the
+  // converters read the packed weight), full_b (the converters wrote B;
+  // implies full_l), mma_done (the UMMAs of the stage finished: frees x and B).
   uint64_t* full_l = bars;
-  uint64_t* empty_l = bars + NL;
-  uint64_t* full_b = bars + 2 * NL;
-  uint64_t* empty_b = bars + 2 * NL + NB;
-  uint64_t* full_acc = bars + 2 * NL + 2 * NB;
+  uint64_t* read_w = bars + NS;
+  uint64_t* full_b = bars + 2 * NS;
+  uint64_t* mma_done = bars + 3 * NS;
+  uint64_t* full_acc = bars + 4 * NS;
   uint64_t* empty_acc = full_acc + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
@@ -228,13 +235,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    for (int i = 0; i < NL; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&full_l[i], 1);
-      mbar_init(&empty_l[i], kConvWarps + 1);
-    }
-    for (int i = 0; i < NB; ++i) {
+      mbar_init(&read_w[i], kConvWarps);
       mbar_init(&full_b[i], kConvWarps);
-      mbar_init(&empty_b[i], 1);
+      mbar_init(&mma_done[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&full_acc[i], 1);
@@ -284,9 +289,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
         int kb_lo, kb_hi;
         unit_kb(u, kb_lo, kb_hi);
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
-          const int s = it % NL;
-          const uint32_t r = it / NL;
-          if (!(ok = mbar_wait(&empty_l[s], (r & 1) ^ 1, p.status, 10, abort_flag))) break;
+          const int s = it % NS;
+          const uint32_t ph = ((it / NS) & 1) ^ 1;  // previous use of the stage
+          if (!(ok = mbar_wait(&read_w[s], ph, p.status, 10, abort_flag))) break;
+          if (!(ok = mbar_wait(&mma_done[s], ph, p.status, 11, abort_flag))) break;
           mbar_arrive_expect_tx(&full_l[s], kXTileBytes + PreFmt<FMT>::kWcBytes);
           tma_load_2d(smem + L::kX + s * kXTileBytes, &xmap, &full_l[s], kb * BK, mt * BM);
           tma_load_2d(smem + L::kWc + s * PreFmt<FMT>::kWcBytes, &wmap, &full_l[s],
@@ -296,15 +302,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
       // let in-flight copies land before the CTA can exit
       if (!ok) {
         const int last = it;
-        for (int j = (last > NL ? last - NL : 0); j < last; ++j) {
-          mbar_wait(&full_l[j % NL], (j / NL) & 1, nullptr, 0, nullptr);
+        for (int j = (last > NS ? last - NS : 0); j < last; ++j) {
+          mbar_wait(&full_l[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
         }
       }
     }
   } else if (warp == kWarpMma) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(BF16, BM, BN);
-      int it_l = 0, it_b = 0, tcount = 0;
+      int it = 0, tcount = 0;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++tcount) {
         const int acc = tcount & 1;
         const uint32_t ar = tcount >> 1;
@@ -313,20 +319,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
         const uint32_t d = tmem_base + acc * BN;
         int kb_lo, kb_hi;
         unit_kb(u, kb_lo, kb_hi);
-        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it_l, ++it_b) {
-          const int sl = it_l % NL, sb = it_b % NB;
-          if (!(ok = mbar_wait(&full_l[sl], (it_l / NL) & 1, p.status, 21, abort_flag))) break;
-          if (!(ok = mbar_wait(&full_b[sb], (it_b / NB) & 1, p.status, 22, abort_flag))) break;
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+          const int s = it % NS;
+          if (!(ok = mbar_wait(&full_b[s], (it / NS) & 1, p.status, 22, abort_flag))) break;
           tc_fence_after();
-          const uint64_t adesc = sw128_kmajor_desc(smem_u32(smem + L::kX + sl * kXTileBytes));
-          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kB + sb * kBTileBytes));
+          const uint64_t adesc = sw128_kmajor_desc(smem_u32(smem + L::kX + s * kXTileBytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kB + s * kBTileBytes));
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             // +32 bytes along K inside the swizzled row = +2 in the address field
             umma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > kb_lo || kk > 0) ? 1u : 0u);
           }
-          tc_commit(&empty_l[sl]);
-          tc_commit(&empty_b[sb]);
+          tc_commit(&mma_done[s]);
         }
         if (!ok) break;
         tc_commit(&full_acc[acc]);
@@ -335,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
   } else if (warp < kWarpEpi0) {
     // ---------------- converters: one weight row per thread ----------------
     const int row = (warp - kWarpConv0) * 32 + lane;  // 0..255
-    int it_l = 0, it_b = 0;
+    int it = 0;
     AwqRowParams<BF16> rp{};
     // AWQ: raw fp16 (scale, zero) of the k-block about to be converted, loaded
     // one k-block ahead so the global-load latency hides behind a conversion
@@ -362,8 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       int kb_lo, kb_hi;
       unit_kb(u, kb_lo, kb_hi);
-      for (int kb = kb_lo; kb < kb_hi; ++kb, ++it_l, ++it_b) {
-        const int sl = it_l % NL, sb = it_b % NB;
+      for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+        const int s = it % NS;
+        const uint32_t ph = (it / NS) & 1;
         if constexpr (FMT == 0) {
           unsigned short nxt_s, nxt_z;
           if (kb + 1 < kb_hi) {
@@ -380,11 +385,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
           cur_s = nxt_s;
           cur_z = nxt_z;
         }
-        if (!(ok = mbar_wait(&full_l[sl], (it_l / NL) & 1, p.status, 30, abort_flag))) break;
-        if (!(ok = mbar_wait(&empty_b[sb], ((it_b / NB) & 1) ^ 1, p.status, 31, abort_flag))) break;
-        const uint32_t wc = smem_u32(smem + L::kWc + sl * PreFmt<FMT>::kWcBytes) +
+        if (!(ok = mbar_wait(&full_l[s], ph, p.status, 30, abort_flag))) break;
+        if (!(ok = mbar_wait(&mma_done[s], ph ^ 1, p.status, 31, abort_flag))) break;
+        const uint32_t wc = smem_u32(smem + L::kWc + s * PreFmt<FMT>::kWcBytes) +
                             row * PreFmt<FMT>::kRowBytes;
-        const uint32_t brow = smem_u32(smem + L::kB + sb * kBTileBytes) + row * 128;
+        const uint32_t brow = smem_u32(smem + L::kB + s * kBTileBytes) + row * 128;
         if constexpr (FMT == 0) {
           // 32-byte swizzle: 16-byte chunk c of row r sits at c ^ ((r >> 2) & 1)
           const uint32_t sw = (row >> 2) & 1;
@@ -420,8 +425,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_linear_kernel(
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&full_b[sb]);
-          mbar_arrive(&empty_l[sl]);
+          mbar_arrive(&read_w[s]);
+          mbar_arrive(&full_b[s]);
         }
       }
     }

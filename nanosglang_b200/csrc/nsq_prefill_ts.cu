@@ -32,10 +32,10 @@
 // Accumulators are double-buffered (the epilogue of tile i overlaps the main
 // loop of tile i + 1). Every wait is bounded.
 #include <atomic>
-#include <type_traits>
 
 #include "nsq_common.cuh"
 #include "nsq_internal.h"
+#include "nsq_tmem_operand.cuh"
 
 namespace nsq {
 
@@ -102,53 +102,6 @@ struct TsParams {
   int bias_dtype;
   int num_w_tiles, num_t_tiles, num_kb;
 };
-
-template <bool BF16>
-struct TsRowDq {  // per-row AWQ dequant constants in the MMA element type
-  uint32_t s2, zb2, magic2, c2;
-  bool exact;
-};
-
-template <bool BF16>
-__device__ __forceinline__ uint32_t ts_pack2(float a, float b) {
-  if constexpr (BF16) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&v);
-  } else {
-    __half2 v = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&v);
-  }
-}
-
-template <bool BF16>
-__device__ __forceinline__ TsRowDq<BF16> ts_row_dq(float s, float z) {
-  TsRowDq<BF16> r;
-  constexpr float kMagic = Magic<BF16>::kValue;
-  constexpr float kZMax = BF16 ? 127.0f : 1023.0f;
-  r.exact = (z == rintf(z)) && fabsf(z) <= kZMax;
-  r.s2 = ts_pack2<BF16>(s, s);
-  r.zb2 = ts_pack2<BF16>(kMagic + z, kMagic + z);
-  r.magic2 = ts_pack2<BF16>(kMagic, kMagic);
-  r.c2 = ts_pack2<BF16>(-z * s, -z * s);
-  return r;
-}
-
-// {magic + q_a, magic + q_b} -> {(q_a - z) s, (q_b - z) s}; exact in the
-// packed domain when z is a small integer, else fma with -z s
-template <bool BF16>
-__device__ __forceinline__ uint32_t ts_dq2(uint32_t e, const TsRowDq<BF16>& rp) {
-  using T2 = typename std::conditional<BF16, __nv_bfloat162, __half2>::type;
-  const T2 ev = *reinterpret_cast<const T2*>(&e);
-  const T2 s = *reinterpret_cast<const T2*>(&rp.s2);
-  T2 o;
-  if (rp.exact) {
-    o = __hmul2(__hsub2(ev, *reinterpret_cast<const T2*>(&rp.zb2)), s);
-  } else {
-    o = __hfma2(__hsub2(ev, *reinterpret_cast<const T2*>(&rp.magic2)), s,
-                *reinterpret_cast<const T2*>(&rp.c2));
-  }
-  return *reinterpret_cast<uint32_t*>(&o);
-}
 
 template <int FMT, bool BF16, int BT>
 __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
@@ -305,8 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         const uint32_t ph = (it / NS) & 1;
         if constexpr (FMT == 0) {
           if ((kb * BK) % p.group_size == 0) {  // a new group (kb = 0 included)
-            rp = ts_row_dq<BF16>(__half2float(__ushort_as_half((unsigned short)(sz0 & 0xFFFFu))),
-                                 __half2float(__ushort_as_half((unsigned short)(sz0 >> 16))));
+            rp = ts_row_dq_packed<BF16>(sz0);
             sz0 = sz1;
             sz1 = sz2;
             sz2 = load_sz();
@@ -314,34 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         }
         if (!(ok = mbar_wait(&full_l[s], ph, p.status, 54, abort_flag))) break;
         uint32_t o[16];
-        if constexpr (FMT == 0) {
-          // 32-byte swizzle: 16-byte chunk c of row r sits at c ^ ((r >> 2) & 1)
-          const uint32_t wc = smem_u32(smem + L::kWc + s * TsFmt<0>::kWcBytes) + row * 32;
-          const uint4 v = lds128(wc + ((half ^ ((row >> 2) & 1)) << 4));
-          const uint32_t words[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            uint32_t e[4];
-            unpack_nibble_pairs<BF16>(words[w], e);
-            // e[t] = {q_t, q_{t+4}} -> in-order pairs {q0,q1},{q2,q3},{q4,q5},{q6,q7}
-            o[4 * w + 0] = ts_dq2<BF16>(prmt(e[0], e[1], 0x5410), rp);
-            o[4 * w + 1] = ts_dq2<BF16>(prmt(e[2], e[3], 0x5410), rp);
-            o[4 * w + 2] = ts_dq2<BF16>(prmt(e[0], e[1], 0x7632), rp);
-            o[4 * w + 3] = ts_dq2<BF16>(prmt(e[2], e[3], 0x7632), rp);
-          }
-        } else {
-          // 64-byte swizzle: 16-byte chunk c of row r sits at c ^ ((r >> 1) & 3)
-          const uint32_t wc = smem_u32(smem + L::kWc + s * TsFmt<1>::kWcBytes) + row * 64;
-          const uint32_t sw = (row >> 1) & 3;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const uint4 v = lds128(wc + (((2 * half + c) ^ sw) << 4));
-            e4m3x4_to_pairs<BF16>(v.x, o[8 * c + 0], o[8 * c + 1]);
-            e4m3x4_to_pairs<BF16>(v.y, o[8 * c + 2], o[8 * c + 3]);
-            e4m3x4_to_pairs<BF16>(v.z, o[8 * c + 4], o[8 * c + 5]);
-            e4m3x4_to_pairs<BF16>(v.w, o[8 * c + 6], o[8 * c + 7]);
-          }
-        }
+        ts_convert_k32<FMT, BF16>(smem_u32(smem + L::kWc + s * TsFmt<FMT>::kWcBytes), row, half, rp, o);
         // the packed tile is consumed (the x tile of the stage is freed by
         // the UMMAs' commit)
         __syncwarp();
@@ -360,7 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
     // ---------------- epilogue: TMEM -> registers -> y ----------------
     const int sub = warp & 3;
     const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
-    const bool pair_ok = (p.N & 1) == 0;
     int tcount = 0;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++tcount) {
       const int wt = u / p.num_t_tiles;
@@ -380,35 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         uint32_t r[32];
         tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_ld_wait();
-        const int mc = m0 + c * 32;
-        if (pair_ok) {
-          // lanes 2i and 2i+1 hold features n, n+1: the even lane stores the
-          // pair of token 2j, the odd lane the pair of token 2j+1
-          const bool odd = lane & 1;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float a0 = __uint_as_float(r[2 * j]), a1 = __uint_as_float(r[2 * j + 1]);
-            const float v0 = has_bias ? fmaf(a0, wscale, bn) : a0 * wscale;
-            const float v1 = has_bias ? fmaf(a1, wscale, bn) : a1 * wscale;
-            const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
-            const int m = mc + 2 * j + (odd ? 1 : 0);
-            const int nn = odd ? n - 1 : n;
-            if (m < p.M && nn < p.N) {
-              const uint32_t w = odd ? ts_pack2<BF16>(recv, v1) : ts_pack2<BF16>(v0, recv);
-              *reinterpret_cast<uint32_t*>(y + (int64_t)m * p.N + nn) = w;
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float a = __uint_as_float(r[j]);
-            const float v = has_bias ? fmaf(a, wscale, bn) : a * wscale;
-            const int m = mc + j;
-            if (m < p.M && n < p.N) {
-              y[(int64_t)m * p.N + n] = static_cast<uint16_t>(ts_pack2<BF16>(v, 0.f) & 0xFFFFu);
-            }
-          }
-        }
+        ts_store_tokens<BF16>(y, p.M, p.N, n, m0 + c * 32, r, wscale, has_bias, bn, lane);
       }
       tc_fence_before();
       __syncwarp();

@@ -1,0 +1,514 @@
+// Prefill-regime quantized linear on a CTA pair with the dequantised weight
+// in tensor memory: y^T = W_deq . x^T with one tcgen05.mma.cta_group::2 of
+// 256 weight rows x 256 tokens x 16 per step. The main large-M path.
+//
+// Replaces AWQLinear.forward / FP8Linear.forward (nano_sglang/decode/
+// quantization.py:150-152, :49-52) for prefill-sized batches.
+//
+// Each CTA of the pair converts its own 128 weight rows straight into its own
+// TMEM (A operand, same address in both CTAs) and stages its own 128 tokens of
+// x in shared memory (B operand, N split over the pair); the accumulator of
+// each CTA holds its 128 weight rows x all 256 tokens. Per CTA and 64-column
+// k-block, shared memory carries 16 KB of x and the packed weight tile (TMA
+// writes, the converters' read and the tensor core's x read: ~48 KB against
+// 512 cycles of MMA), and the conversion of a weight row is shared by 256
+// tokens.
+//
+// Warp roles (both CTAs, 608 threads each):
+//   warp 0        TMA producer: x tile [128 tokens x 64] (128-byte swizzle)
+//                 and this CTA's packed weight tile [128 rows x 64 columns],
+//                 KPS of each per stage, NS-stage ring, completion on this
+//                 CTA's own barrier.
+//   warp 1        TMEM allocation (512 columns, paired); in the even CTA, lane
+//                 0 issues the UMMAs and the multicast commits.
+//   warp 2        forwarder: once this CTA's converters finished a stage, one
+//                 arrival on the even CTA's operand barrier (a single
+//                 cluster-scope arrival per CTA and stage).
+//   warps 3..10   converters: warp w serves TMEM sub-partition w % 4 (32
+//                 weight rows, one per lane) and half (w - 3) / 4 of the 64
+//                 columns; tcgen05.st into an NS-stage TMEM operand ring.
+//   warps 11..18  epilogue: two warps per TMEM sub-partition (128 tokens
+//                 each), tcgen05.ld of the accumulator (lane = output feature,
+//                 column = token), scale (FP8), bias, rounding into a staged
+//                 [tokens][features] tile, TMA stores of y.
+// A stage holds KPS k-blocks, so each round of barrier operations in the UMMA
+// issuer (a wait and a commit, ~300 cycles in which the tensor pipe drains on
+// B200) covers 8 UMMAs. The single accumulator (256 columns) leaves the other
+// 256 TMEM columns to the operand ring; the UMMAs of the next tile start once
+// both CTAs' epilogues have drained theirs into shared memory, and the y
+// stores overlap them. Every wait is bounded; no TMA multicast.
+#include <atomic>
+
+#include "nsq_common.cuh"
+#include "nsq_internal.h"
+#include "nsq_tmem_operand.cuh"
+
+namespace nsq {
+
+namespace {
+
+constexpr int BWC = 128;  // weight rows per CTA (TMEM lanes); the pair tile is 256
+constexpr int BTP = 256;  // tokens per pair tile (UMMA N); 128 per CTA
+constexpr int BK = 64;
+constexpr int KPS = 2;    // k-blocks per stage: one barrier round per 8 UMMAs
+constexpr int kWarpTma = 0;
+constexpr int kWarpMma = 1;
+constexpr int kWarpFwd = 2;
+constexpr int kWarpConv0 = 3;
+constexpr int kConvWarps = 8;
+constexpr int kWarpEpi0 = kWarpConv0 + kConvWarps;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = BTP;  // operand stages start after the accumulator
+constexpr int kXBytes = (BTP / 2) * BK * 2;  // one k-block of x: 16 KB per CTA
+
+// Stages (x + packed weight in shared memory, operand in TMEM): 4, or 3 for
+// FP8 when the staged y tile (64 KB) has to fit beside them.
+__host__ __device__ constexpr int ts2_stages(int fmt, bool staged) { return (fmt == 1 && staged) ? 3 : 4; }
+
+template <int FMT, bool STAGED>
+struct Ts2Smem {
+  static constexpr int NS = ts2_stages(FMT, STAGED);
+  static_assert(kTmemA + NS * KPS * 32 <= kTmemCols, "tensor memory budget");
+  static constexpr int kWcBytes = FMT == 0 ? BWC * BK / 2 : BWC * BK;
+  static constexpr int kX = 0;                          // [NS][KPS] x tiles
+  static constexpr int kWc = kX + NS * KPS * kXBytes;   // [NS][KPS] packed weight tiles
+  static constexpr int kY = kWc + NS * KPS * kWcBytes;  // staged y tile: 2 x [256 tokens][64 features]
+  static constexpr int kYHalfBytes = BTP * 64 * 2;
+  static constexpr int kBar = kY + (STAGED ? 2 * kYHalfBytes : 0);
+  // full_l[NS], read_w[NS], conv_done[NS], full_a[NS], mma_done[NS], full_acc, empty_acc
+  static constexpr int kNumBars = 5 * NS + 2;
+  static constexpr int kTmemSlot = kBar + kNumBars * 8;
+  static constexpr int kAbort = kTmemSlot + 4;
+  static constexpr int kTotal = kAbort + 4;
+  static constexpr int kAlloc = kTotal + 1024;
+  static_assert(kAlloc <= 227 * 1024, "shared memory per CTA");
+  static_assert(kY % 1024 == 0, "staged y tile stays 1 KB aligned (128-byte swizzle)");
+};
+
+struct Ts2Params {
+  const __half* scales;
+  const __half* zeros;
+  const float* wscale;
+  const void* bias;
+  void* y;
+  DevStatus* status;
+  int M, K, N;
+  int group_size, G;
+  int bias_dtype;
+  int num_w_tiles, num_t_tiles, num_kb;  // w tiles of 256 rows, t tiles of 256 tokens
+  int num_st;                            // stages per tile: ceil(num_kb / KPS)
+};
+
+// tokens of pair tile tt given to the UMMA (N): all 256, or the remainder
+// rounded up to 32 (paired N is a multiple of 32; x rows past M read as zero)
+__device__ __forceinline__ int ts2_n_eff(int M, int tt) {
+  const int rem = M - tt * BTP;
+  return rem >= BTP ? BTP : ((rem + 31) & ~31);
+}
+
+template <int FMT, bool BF16, bool STAGED>
+__global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
+    const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+    const __grid_constant__ CUtensorMap ymap, const Ts2Params p) {
+  using L = Ts2Smem<FMT, STAGED>;
+  constexpr int NS = L::NS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  // Per stage s (both CTAs unless noted): full_l (this CTA's x and packed
+  // weight bytes), read_w (this CTA's converters read the packed weight),
+  // conv_done (this CTA's converters wrote its TMEM operand; implies full_l),
+  // full_a (even CTA: one arrival per CTA's forwarder), mma_done (multicast
+  // commit: frees the x tile and the TMEM operand in both CTAs).
+  uint64_t* full_l = bars;
+  uint64_t* read_w = bars + NS;
+  uint64_t* conv_done = bars + 2 * NS;
+  uint64_t* full_a = bars + 3 * NS;
+  uint64_t* mma_done = bars + 4 * NS;
+  uint64_t* full_acc = bars + 5 * NS;
+  uint64_t* empty_acc = full_acc + 1;  // even CTA: every epilogue warp of both CTAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1;
+  const int ncl = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full_l[i], 1);
+      mbar_init(&read_w[i], kConvWarps);
+      mbar_init(&conv_done[i], kConvWarps);
+      mbar_init(&full_a[i], 2);
+      mbar_init(&mma_done[i], 1);
+    }
+    mbar_init(full_acc, 1);
+    mbar_init(empty_acc, 2 * kEpiWarps);
+    fence_barrier_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers and TMEM exist before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  pdl_wait_prior_grids();
+
+  const int num_units = p.num_w_tiles * p.num_t_tiles;  // token tile fastest
+  bool ok = true;
+
+  if (warp == kWarpTma) {
+    if (lane == 0) {
+      tma_prefetch_desc(&xmap);
+      tma_prefetch_desc(&wmap);
+      int it = 0;
+      for (int u = cid; u < num_units && ok; u += ncl) {
+        const int wt = u / p.num_t_tiles;
+        const int tt = u - wt * p.num_t_tiles;
+        // this CTA's tokens: the second half of the UMMA's N starts at n_eff / 2
+        const int tok0 = tt * BTP + (int)rank * (ts2_n_eff(p.M, tt) >> 1);
+        for (int st = 0; st < p.num_st; ++st, ++it) {
+          const int s = it % NS;
+          const uint32_t ph = ((it / NS) & 1) ^ 1;  // previous use of the stage
+          if (!(ok = mbar_wait(&read_w[s], ph, p.status, 150, abort_flag))) break;
+          if (!(ok = mbar_wait(&mma_done[s], ph, p.status, 151, abort_flag))) break;
+          const int kb0 = st * KPS;
+          const int nk = p.num_kb - kb0 < KPS ? p.num_kb - kb0 : KPS;
+          mbar_arrive_expect_tx(&full_l[s], (uint32_t)nk * (kXBytes + L::kWcBytes));
+          for (int i = 0; i < nk; ++i) {
+            const int kb = kb0 + i;
+            tma_load_2d(smem + L::kX + (s * KPS + i) * kXBytes, &xmap, &full_l[s], kb * BK, tok0);
+            tma_load_2d(smem + L::kWc + (s * KPS + i) * L::kWcBytes, &wmap, &full_l[s],
+                        FMT == 0 ? kb * (BK / 8) : kb * BK, wt * (2 * BWC) + (int)rank * BWC);
+          }
+        }
+      }
+      if (!ok) {  // let in-flight copies land before the CTA can exit
+        for (int j = (it > NS ? it - NS : 0); j < it; ++j) {
+          mbar_wait(&full_l[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
+        }
+      }
+    }
+  } else if (warp == kWarpMma) {
+    if (leader && lane == 0) {
+      int it = 0, tcount = 0;
+      for (int u = cid; u < num_units && ok; u += ncl, ++tcount) {
+        const int tt = u % p.num_t_tiles;
+        const uint32_t idesc = umma_idesc_f16(BF16, 2 * BWC, ts2_n_eff(p.M, tt));
+        if (!(ok = mbar_wait(empty_acc, (tcount & 1) ^ 1, p.status, 152, abort_flag))) break;
+        tc_fence_after();
+        for (int st = 0; st < p.num_st; ++st, ++it) {
+          const int s = it % NS;
+          if (!(ok = mbar_wait(&full_a[s], (it / NS) & 1, p.status, 153, abort_flag))) break;
+          tc_fence_after();
+          const int nk = p.num_kb - st * KPS < KPS ? p.num_kb - st * KPS : KPS;
+#pragma unroll
+          for (int i = 0; i < KPS; ++i) {
+            if (i < nk) {
+              const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kX + (s * KPS + i) * kXBytes));
+              const uint32_t a = tmem_base + kTmemA + (s * KPS + i) * 32;
+#pragma unroll
+              for (int kk = 0; kk < BK / 16; ++kk) {
+                // A: +8 TMEM columns per 16 K; B: +32 bytes inside the swizzled row
+                umma_f16_pair_ts(tmem_base, a + 8 * kk, bdesc + 2 * kk, idesc, (st > 0 || i > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+          }
+          tc_commit_pair_mc(&mma_done[s], 0x3);
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(full_acc, 0x3);
+      }
+    }
+  } else if (warp == kWarpFwd) {
+    if (lane == 0) {
+      const uint32_t full_a_leader0 = dsmem_map(smem_u32(&full_a[0]), 0);
+      const int total = ((num_units - cid + ncl - 1) / ncl) * p.num_st;
+      for (int it = 0; it < total; ++it) {
+        const int s = it % NS;
+        if (!(ok = mbar_wait(&conv_done[s], (it / NS) & 1, p.status, 154, abort_flag))) break;
+        mbar_arrive_cluster(full_a_leader0 + s * 8);
+      }
+    }
+  } else if (warp < kWarpEpi0) {
+    // ---------------- converters: packed weight -> TMEM operand ----------------
+    const int sub = warp & 3;                   // TMEM sub-partition = 32 weight rows
+    const int half = (warp - kWarpConv0) >> 2;  // 32-column half of the k-block
+    const int row = sub * 32 + lane;            // weight row within this CTA's 128
+    const uint32_t a_lane = tmem_base + ((uint32_t)(sub * 32) << 16) + kTmemA + half * 16;
+    // AWQ: (scale, zero) of this thread's row, in the order of use, loaded
+    // three groups ahead into a register ring
+    const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
+    const unsigned short* zr16 = reinterpret_cast<const unsigned short*>(p.zeros);
+    int pu = cid, pg = 0;
+    auto load_sz = [&]() -> uint32_t {
+      uint32_t v = 0;
+      if (pu < num_units) {
+        const int n = (pu / p.num_t_tiles) * (2 * BWC) + (int)rank * BWC + row;
+        if (n < p.N) {
+          const int64_t off = (int64_t)n * p.G + pg;
+          v = (uint32_t)__ldg(sc16 + off) | ((uint32_t)__ldg(zr16 + off) << 16);
+        }
+        if (++pg == p.G) {
+          pg = 0;
+          pu += ncl;
+        }
+      }
+      return v;
+    };
+    uint32_t sz0 = 0, sz1 = 0, sz2 = 0;
+    if constexpr (FMT == 0) {
+      sz0 = load_sz();
+      sz1 = load_sz();
+      sz2 = load_sz();
+    }
+    TsRowDq<BF16> rp{};
+    int it = 0;
+    for (int u = cid; u < num_units && ok; u += ncl) {
+      for (int st = 0; st < p.num_st; ++st, ++it) {
+        const int s = it % NS;
+        const uint32_t ph = (it / NS) & 1;
+        if (!(ok = mbar_wait(&full_l[s], ph, p.status, 155, abort_flag))) break;
+        // the TMEM operand stage is free once the UMMAs of its previous use finished
+        if (!(ok = mbar_wait(&mma_done[s], ph ^ 1, p.status, 156, abort_flag))) break;
+        tc_fence_after();
+        const int nk = p.num_kb - st * KPS < KPS ? p.num_kb - st * KPS : KPS;
+#pragma unroll
+        for (int i = 0; i < KPS; ++i) {
+          if (i < nk) {
+            if constexpr (FMT == 0) {
+              if (((st * KPS + i) * BK) % p.group_size == 0) {  // a new group (k-block 0 included)
+                rp = ts_row_dq_packed<BF16>(sz0);
+                sz0 = sz1;
+                sz1 = sz2;
+                sz2 = load_sz();
+              }
+            }
+            uint32_t o[16];
+            ts_convert_k32<FMT, BF16>(smem_u32(smem + L::kWc + (s * KPS + i) * L::kWcBytes), row, half, rp, o);
+            tmem_st_32x32b_x16(a_lane + (s * KPS + i) * 32, o);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&read_w[s]);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv_done[s]);
+      }
+    }
+  } else {
+    // ---------------- epilogue: TMEM -> registers -> staged tile -> TMA store ----------------
+    // STAGED: the accumulator is drained into shared memory (bf16/fp16, two
+    // 128-byte-swizzled [256 tokens][64 features] halves) and released at
+    // once; the TMA stores of the tile overlap the next tile's UMMAs. Else the
+    // lanes store y directly (long K, where a deeper ring is worth more, or
+    // N % 8 != 0: no 16-byte row pitch for a tensor map).
+    const int sub = warp & 3;
+    const int chalf = (warp - kWarpEpi0) >> 2;  // tokens [128 chalf, 128 chalf + 128) of the tile
+    const int etid = threadIdx.x - kWarpEpi0 * 32;
+    const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
+    const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;
+    const uint32_t empty_acc_leader = dsmem_map(smem_u32(empty_acc), 0);
+    uint16_t* y = static_cast<uint16_t*>(p.y);
+    // staged position of this lane's feature: half (sub / 2), 16-byte chunk and byte in the row
+    const int fl = (sub & 1) * 32 + lane;
+    const uint32_t ystage = smem_u32(smem + L::kY + (sub >> 1) * L::kYHalfBytes);
+    const uint32_t ychunk = (uint32_t)(fl >> 3);
+    const uint32_t ybyte = (uint32_t)((fl & 6) * 2);  // the pair (f & ~1, f | 1) starts here
+    const bool odd = lane & 1;
+    int tcount = 0;
+    for (int u = cid; u < num_units && ok; u += ncl, ++tcount) {
+      const int wt = u / p.num_t_tiles;
+      const int tt = u - wt * p.num_t_tiles;
+      ok = mbar_wait(full_acc, tcount & 1, p.status, 157, abort_flag);
+      if (!named_bar_all(1, kEpiWarps * 32, ok)) {  // leave together if anyone gave up
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int n = wt * (2 * BWC) + (int)rank * BWC + sub * 32 + lane;  // this thread's output feature
+      const float bn = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+      const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16) + chalf * 128;
+      const int m0 = tt * BTP + chalf * 128;  // accumulator column c holds token tt * 256 + c
+      if constexpr (STAGED) {
+        // the previous tile's stores have read the staged tile
+        if (etid == 0) bulk_wait_group_read<0>();
+        named_bar_sync(1, kEpiWarps * 32);
+#pragma unroll 1
+        for (int c = 0; c < 4 && m0 + c * 32 < p.M; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_ld_wait();
+          // lanes 2i, 2i+1 (features f, f+1) exchange values: the even lane
+          // stages the pair of token a, the odd lane that of token a + 4
+          // (rows 4 apart fall on different chunk swizzles: no bank conflicts)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int a = (j >> 2) * 8 + (j & 3);
+            const float va = has_bias ? fmaf(__uint_as_float(r[a]), wscale, bn) : __uint_as_float(r[a]) * wscale;
+            const float vb =
+                has_bias ? fmaf(__uint_as_float(r[a + 4]), wscale, bn) : __uint_as_float(r[a + 4]) * wscale;
+            const float recv = __shfl_xor_sync(0xffffffffu, odd ? va : vb, 1);
+            const uint32_t t = (uint32_t)(chalf * 128 + c * 32 + a + (odd ? 4 : 0));  // staged row
+            const uint32_t w = odd ? ts_pack2<BF16>(recv, vb) : ts_pack2<BF16>(va, recv);
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(ystage + t * 128 + ((ychunk ^ (t & 7)) << 4) + ybyte),
+                         "r"(w)
+                         : "memory");
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_acc_leader);  // the accumulator is free
+        fence_proxy_async_smem();
+        named_bar_sync(1, kEpiWarps * 32);
+        if (etid == 0) {
+          for (int h = 0; h < 2; ++h) {
+            const int f0 = wt * (2 * BWC) + (int)rank * BWC + h * 64;
+            if (f0 < p.N) tma_store_2d(&ymap, smem + L::kY + h * L::kYHalfBytes, f0, tt * BTP);
+          }
+          bulk_commit_group();
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4 && m0 + c * 32 < p.M; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_ld_wait();
+          ts_store_tokens<BF16>(y, p.M, p.N, n, m0 + c * 32, r, wscale, has_bias, bn, lane);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(empty_acc_leader);
+      }
+    }
+    if (STAGED && etid == 0) bulk_wait_group<0>();  // the staged tiles are written out
+  }
+
+  pdl_launch_dependents();
+  __syncthreads();
+  tc_fence_before();
+  cluster_sync_all();  // the pair is done with both CTAs' TMEM and barriers
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+template <int FMT, bool BF16, bool STAGED>
+cudaError_t launch_ts2(const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& ymap,
+                       const Ts2Params& p, int grid, cudaStream_t stream) {
+  using L = Ts2Smem<FMT, STAGED>;
+  auto kern = prefill_ts2_kernel<FMT, BF16, STAGED>;
+  static std::atomic<bool> configured{false};
+  if (!configured.load()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured.store(true);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  attrs[na].id = cudaLaunchAttributeClusterDimension;
+  attrs[na].val.clusterDim.x = 2;
+  attrs[na].val.clusterDim.y = 1;
+  attrs[na].val.clusterDim.z = 1;
+  ++na;
+  if (pdl_enabled()) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, xmap, wmap, ymap, p);
+}
+
+}  // namespace
+
+int run_prefill_ts2_linear(const LinearArgs& a, cudaStream_t stream) {
+  if (a.M <= 0 || a.N <= 0) return NSQ_OK;
+  CUtensorMap xmap, wmap;
+  CUresult cr = encode_tensor_map_2d(
+      &xmap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+      const_cast<void*>(a.x), (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, BK, BTP / 2,
+      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  if (a.fmt == 0) {
+    cr = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<void*>(a.wq),
+                              (uint64_t)a.K / 8, (uint64_t)a.N, (uint64_t)a.K / 2, BK / 8, BWC,
+                              CU_TENSOR_MAP_SWIZZLE_32B);
+  } else {
+    cr = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, const_cast<void*>(a.wq),
+                              (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, BK, BWC,
+                              CU_TENSOR_MAP_SWIZZLE_64B);
+  }
+  if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  // y: [M][N] in the activation dtype, stored as [256 tokens][64 features]
+  // boxes from the staged tile when N % 8 == 0 and the tiles are short in K
+  // (measured on B200: the staged epilogue pays for its smaller ring below
+  // ~16 stages per tile for FP8; AWQ keeps 4 stages either way)
+  CUtensorMap ymap = xmap;
+  const int num_st = ((a.K + BK - 1) / BK + KPS - 1) / KPS;
+  const bool staged = (a.N % 8) == 0 && (a.fmt == 0 || num_st < 16);
+  if (staged) {
+    cr = encode_tensor_map_2d(&ymap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              a.y, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.N * 2, 64, BTP,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  }
+  Ts2Params p{};
+  p.scales = reinterpret_cast<const __half*>(a.scales);
+  p.zeros = reinterpret_cast<const __half*>(a.zeros);
+  p.wscale = a.wscale;
+  p.bias = a.bias;
+  p.y = a.y;
+  p.status = device_status_ptr();
+  p.M = a.M;
+  p.K = a.K;
+  p.N = a.N;
+  p.group_size = a.group_size;
+  p.G = a.fmt == 0 ? (a.K + a.group_size - 1) / a.group_size : 0;
+  p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
+  p.num_w_tiles = (a.N + 2 * BWC - 1) / (2 * BWC);
+  p.num_t_tiles = (a.M + BTP - 1) / BTP;
+  p.num_kb = (a.K + BK - 1) / BK;
+  p.num_st = num_st;
+  const int units = p.num_w_tiles * p.num_t_tiles;
+  const int pairs = num_sms() / 2;
+  const int grid = 2 * (units < pairs ? units : pairs);
+  cudaError_t e;
+  if (a.fmt == 0) {
+    if (staged) {
+      e = a.x_bf16 ? launch_ts2<0, true, true>(xmap, wmap, ymap, p, grid, stream)
+                   : launch_ts2<0, false, true>(xmap, wmap, ymap, p, grid, stream);
+    } else {
+      e = a.x_bf16 ? launch_ts2<0, true, false>(xmap, wmap, ymap, p, grid, stream)
+                   : launch_ts2<0, false, false>(xmap, wmap, ymap, p, grid, stream);
+    }
+  } else {
+    if (staged) {
+      e = a.x_bf16 ? launch_ts2<1, true, true>(xmap, wmap, ymap, p, grid, stream)
+                   : launch_ts2<1, false, true>(xmap, wmap, ymap, p, grid, stream);
+    } else {
+      e = a.x_bf16 ? launch_ts2<1, true, false>(xmap, wmap, ymap, p, grid, stream)
+                   : launch_ts2<1, false, false>(xmap, wmap, ymap, p, grid, stream);
+    }
+  }
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+}  // namespace nsq
