@@ -27,7 +27,7 @@ column-parallel, o/down row-parallel + NCCL all_reduce; max-over-ranks time.
 --impl reference: the CPU oracle alone on the same workload (rank 0 only).
 --ncu-case NAME: run a few launches of one kernel class and exit (no timing,
 no JSON), for Nsight Compute captures of a small case:
-  prefill        FP8 gate shape, M=16384 (tcgen05 paired-CTA GEMM), 3 launches
+  prefill        FP8 gate shape, M=16384 (paired-CTA TMEM-operand GEMM), 3 launches
   sweep_prefill  the sweep's M > 64 linears once each (the roofline kernel's launches)
   decode         the sweep's M <= 64 linears once each
   awq0           config-0 AWQ linear (M=16, K=896, N=9728), 4 launches

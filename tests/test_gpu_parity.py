@@ -222,6 +222,18 @@ def test_awq_linear_small_output_shapes(m, n, k, gs, zm):
     assert err <= GEMM_TOL, err
 
 
+@pytest.mark.parametrize("m,n,k,gs,zm", [(300, 4104, 896, 128, "frac"), (777, 2050, 1024, 256, "wide"),
+                                         (1024, 4864, 4096, 128, "int")])
+def test_awq_linear_paired_tmem_kernel_shapes(m, n, k, gs, zm):
+    """Outputs beyond 2^20 on the paired-CTA TMEM-operand kernel (AWQ keeps the
+    staged epilogue and a 4-stage ring): ragged token tiles, N % 8 != 0,
+    groups of 2 and 4 k-blocks across two-k-block stages."""
+    err = _awq_case(m, n, k, gs, torch.bfloat16, bias=(m % 2 == 0), zm=zm, seed=m * 5 + n)
+    assert err <= GEMM_TOL, err
+    err = _awq_case(m, n, k, gs, torch.float16, bias=(m % 2 == 1), zm=zm, seed=m * 5 + n + 1)
+    assert err <= GEMM_TOL, err
+
+
 def test_awq_linear_fp16_matches_reference_forward_golden():
     """The reference's own fp16 forward outputs (cases the kernels support)."""
     from nanosglang_b200 import ops
@@ -293,6 +305,15 @@ def test_fp8_linear_fp16_and_odd_shapes(m):
 def test_fp8_linear_small_output_shapes(m, n, k):
     """Prefill problems with at most 2^20 outputs (the TMEM-operand kernel):
     ragged token tiles, odd N, a partial last k-block, bias, fp16."""
+    assert _fp8_case(m, n, k, torch.bfloat16, bias=(m % 2 == 1), seed=m + n) <= GEMM_TOL
+    assert _fp8_case(m, n, k, torch.float16, bias=(m % 2 == 0), seed=m + n + 1) <= GEMM_TOL
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 4104, 896), (777, 2050, 1024), (1024, 4864, 4096), (257, 8200, 512)])
+def test_fp8_linear_paired_tmem_kernel_shapes(m, n, k):
+    """Outputs beyond 2^20 on the paired-CTA TMEM-operand kernel: ragged last
+    token tiles (the odd CTA's half starts at n_eff / 2), N % 8 != 0 (direct
+    stores), long K (deeper ring, direct stores), staged TMA stores."""
     assert _fp8_case(m, n, k, torch.bfloat16, bias=(m % 2 == 1), seed=m + n) <= GEMM_TOL
     assert _fp8_case(m, n, k, torch.float16, bias=(m % 2 == 0), seed=m + n + 1) <= GEMM_TOL
 
