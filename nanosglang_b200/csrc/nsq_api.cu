@@ -200,16 +200,12 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     rc = run_decode_wave_linear(a, stream);
     if (rc != NSQ_ENOTSUP) return rc;
   }
-  // Prefill: the one-CTA GEMM with K split over a thread-block cluster when
-  // its 128 x 256 tiles leave most SMs idle and K is long; else the weight
-  // tile dequantised into tensor memory -- one CTA per 128 rows for small
-  // outputs, CTA pairs (256 rows x 256 tokens) for the rest.
-  if (prefill_split_factor(a.M, a.K, a.N) == 1) {
-    const int bt = prefill_ts_tokens_per_tile(a.M, a.K, a.N);
-    if (bt > 0) return run_prefill_ts_linear(a, bt, stream);
-    return run_prefill_ts2_linear(a, stream);
-  }
-  return run_prefill_linear(a, stream);
+  // Prefill: the weight tile dequantised into tensor memory -- one CTA per
+  // 128 rows (K split over a cluster when the tiles are few) for problems
+  // that 256 x 256 pair tiles would leave mostly idle, CTA pairs otherwise.
+  const TsPlan tp = prefill_ts_plan(a.M, a.K, a.N);
+  if (tp.tokens_per_tile > 0) return run_prefill_ts_linear(a, tp, stream);
+  return run_prefill_ts2_linear(a, stream);
 }
 
 int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,

@@ -52,14 +52,16 @@ int run_decode_wave_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 6
 int run_decode_stream_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 64, persistent weight ring
 int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64, one or more waves
 int decode_linear_ctas(const LinearArgs& a);  // CTAs run_decode_linear launches, -1 if it cannot
-int run_prefill_linear(const LinearArgs& a, cudaStream_t stream);  // any M, one CTA per tile (K split over a cluster when few tiles)
-int prefill_split_factor(int64_t M, int64_t K, int64_t N);      // CTAs per tile along K (1: no split)
-// weight tile dequantised into tensor memory (A operand), tokens as UMMA N;
-// tokens_per_tile 64, 128 or 192
-int run_prefill_ts_linear(const LinearArgs& a, int tokens_per_tile, cudaStream_t stream);
-int prefill_ts_tokens_per_tile(int64_t M, int64_t K, int64_t N);  // 0: use the other prefill kernels
-// CTA pairs, weight tile dequantised into each CTA's tensor memory, 256 weight
-// rows x 256 tokens per pair tile
+// prefill: the weight tile dequantised into tensor memory (A operand), tokens
+// as UMMA N. One CTA per 128 weight rows x 64/128 tokens, K optionally split
+// over a cluster (small outputs, few-tile long-K layers), or CTA pairs with
+// 256 weight rows x 256 tokens (the rest).
+struct TsPlan {
+  int tokens_per_tile;  // 64 or 128; 0: use the paired kernel
+  int ksplit;           // CTAs per tile along K (cluster size)
+};
+TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N);
+int run_prefill_ts_linear(const LinearArgs& a, TsPlan plan, cudaStream_t stream);
 int run_prefill_ts2_linear(const LinearArgs& a, cudaStream_t stream);
 
 constexpr int kDecodeMaxM = 64;

@@ -1,36 +1,43 @@
-// Prefill-regime quantized linear with the dequantised weight tile held in
-// tensor memory: the transposed product y^T = W_deq . x^T on tcgen05, A
-// operand (128 weight rows) read from TMEM, B operand (the token tile of x)
-// from shared memory.
+// Prefill-regime quantized linear, one CTA per 128 weight rows, with the
+// dequantised weight tile held in tensor memory: y^T = W_deq . x^T on
+// tcgen05, A operand (128 weight rows) read from TMEM, B operand (the token
+// tile of x, 64 or 128 tokens) from shared memory.
 //
 // Replaces AWQLinear.forward / FP8Linear.forward (nano_sglang/decode/
-// quantization.py:150-152, :49-52) for prefill-sized batches whose tiles the
-// shared-memory-operand kernels cannot spread over the GPU (few tokens, or few
-// output features), and wherever it is measured faster.
+// quantization.py:150-152, :49-52) for prefill-sized problems too small to
+// fill the GPU with the paired kernel's 256 x 256 tiles: small outputs (q/k/v
+// at M = 128 .. 1024, k/v at M = 8192) and long-K layers with few tiles
+// (down at M <= 1024), whose K range is then split over the CTAs of a
+// thread-block cluster.
 //
 // Why TMEM for the weight: with both operands in shared memory, a 64-column
-// K step of a 128 x 256 tile moves ~128 KB through shared memory (TMA writes
-// of x and the packed weight, the converters' read of the packed weight and
-// write of the converted one, the tensor core's operand reads) -- about twice
-// the MMA time of that step. The converted weight here goes from registers
-// straight into tensor memory (tcgen05.st); shared memory carries only x and
-// the packed weight.
+// K step moves the converted weight through shared memory twice more than the
+// tensor core needs; here the converters write it from registers straight
+// into tensor memory (tcgen05.st) and shared memory carries only x and the
+// packed weight.
 //
 // Warp roles, 448 threads:
-//   warp 0        TMA producer: x tile [BT tokens x 64] (128-byte swizzle) and
-//                 the packed weight tile [128 rows x 64 columns] of the
-//                 reference layout, NS-stage ring.
+//   warp 0        TMA producer: per stage KPS x tiles [BT tokens x 64]
+//                 (128-byte swizzle) and KPS packed weight tiles [128 rows x
+//                 64 columns] of the reference layout, NS-stage ring.
 //   warp 1        TMEM allocation; lane 0 issues 128 x BT x 16 UMMAs with A
-//                 from TMEM and commits the barriers that free the stages.
+//                 from TMEM; one barrier wait and one commit per stage (8
+//                 UMMAs): each barrier operation in the issuer opens a bubble
+//                 of a few hundred cycles in the tensor pipe on B200.
 //   warps 2..9    converters: warp w serves TMEM sub-partition w % 4 (32 weight
-//                 rows, one per lane) and half (w - 2) / 4 of the 64 columns;
+//                 rows, one per lane) and half (w - 2) / 4 of each k-block;
 //                 int4 with zero point and group scale (AWQ) or e4m3 (FP8) ->
-//                 MMA element type -> tcgen05.st into an NS-stage TMEM ring.
+//                 MMA element type -> tcgen05.st into the TMEM operand ring.
 //   warps 10..13  epilogue: tcgen05.ld of the accumulator (lane = output
 //                 feature, column = token), per-tensor scale (FP8), bias,
 //                 rounding, stores of feature pairs exchanged between lanes.
-// Accumulators are double-buffered (the epilogue of tile i overlaps the main
-// loop of tile i + 1). Every wait is bounded.
+// Without a K split the accumulators are double-buffered (the epilogue of tile
+// i overlaps the main loop of tile i + 1). With a K split of ks CTAs per tile
+// (a cluster), every CTA owns BT / ks token columns of the tile: after the
+// main loops it sends its other fp32 columns into the owners' idle x rings
+// (st.async counted on the owner's transaction barrier) and sums the partials
+// of its own columns in rank order, so the result does not depend on timing.
+// Every wait is bounded.
 #include <atomic>
 
 #include "nsq_common.cuh"
@@ -43,7 +50,8 @@ namespace {
 
 constexpr int BW = 128;  // weight rows per tile (UMMA M, TMEM lanes)
 constexpr int BK = 64;   // columns per k-block
-constexpr int NS = 4;    // stages: x tile + packed weight tile in shared memory, operand in TMEM
+constexpr int KPS = 2;   // k-blocks per stage
+constexpr int NS = 4;    // stages
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpConv0 = 2;
@@ -52,6 +60,7 @@ constexpr int kWarpEpi0 = kWarpConv0 + kConvWarps;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
 constexpr int kMinSmem = 120 * 1024;  // keeps one CTA (and one TMEM owner) per SM
+constexpr int kXChunk = 16;           // token columns per exchanged chunk (split K)
 
 template <int FMT>
 struct TsFmt;
@@ -66,21 +75,21 @@ struct TsFmt<1> {  // FP8: 128 rows x 64 B, 64-byte swizzle
 
 template <int BT>
 struct TsTmem {
-  static constexpr uint32_t kAcc = 0;           // 2 accumulators of BT columns
-  static constexpr uint32_t kA = 2 * BT;        // NS operand stages of 32 columns (64 K values)
-  static constexpr uint32_t kUsed = kA + NS * 32;
+  static constexpr uint32_t kAcc = 0;         // 2 accumulators of BT columns
+  static constexpr uint32_t kA = 2 * BT;      // NS operand stages of KPS x 32 columns
+  static constexpr uint32_t kUsed = kA + NS * KPS * 32;
   static constexpr uint32_t kCols = kUsed <= 256 ? 256 : 512;
   static_assert(kUsed <= 512, "tensor memory budget");
 };
 
 template <int FMT, int BT>
 struct TsSmem {
-  static constexpr int kXBytes = BT * BK * 2;
-  static constexpr int kX = 0;
-  static constexpr int kWc = kX + NS * kXBytes;
-  static constexpr int kBar = kWc + NS * TsFmt<FMT>::kWcBytes;
-  // full_l[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc[2], empty_acc[2]
-  static constexpr int kNumBars = 4 * NS + 4;
+  static constexpr int kXBytes = BT * BK * 2;               // one k-block of x
+  static constexpr int kX = 0;                              // [NS][KPS] x tiles
+  static constexpr int kWc = kX + NS * KPS * kXBytes;       // [NS][KPS] packed weight tiles
+  static constexpr int kBar = kWc + NS * KPS * TsFmt<FMT>::kWcBytes;
+  // full_l[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc[2], empty_acc[2], recv
+  static constexpr int kNumBars = 4 * NS + 5;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kTotal = kAbort + 4;
@@ -88,6 +97,8 @@ struct TsSmem {
   static constexpr int kAlloc = kNeed > kMinSmem ? kNeed : kMinSmem;
   static_assert(kXBytes % 1024 == 0, "x stages stay 1 KB aligned");
   static_assert(kAlloc <= 227 * 1024, "shared memory per CTA");
+  // split K: the partial tiles of all ranks (BW x BT fp32) fit in the x ring
+  static_assert(kWc - kX >= BW * BT * 4, "split-K receive slots");
 };
 
 struct TsParams {
@@ -101,7 +112,16 @@ struct TsParams {
   int group_size, G;
   int bias_dtype;
   int num_w_tiles, num_t_tiles, num_kb;
+  int ksplit;  // CTAs per tile along K = cluster size (1: no split)
 };
+
+// Offset of 16-byte unit u of row r in a split-K receive slot whose rows hold
+// `units` units (4 per 16-column chunk): XOR-swizzled so that the eight rows a
+// quarter-warp stores hit eight different bank groups.
+__device__ __forceinline__ uint32_t ts_slot_unit(uint32_t u, uint32_t r, uint32_t units) {
+  if (units >= 8) return ((u & ~7u) | ((u & 7u) ^ (r & 7u))) << 4;
+  return (u ^ ((r >> 1) & 3u)) << 4;  // 64-byte rows: two rows per 128 bytes
+}
 
 template <int FMT, bool BF16, int BT>
 __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
@@ -115,20 +135,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   // Per stage s: full_l (TMA bytes of x and the packed weight landed), read_w
   // (the converters read the packed weight), full_a (the converters wrote the
   // TMEM operand; implies full_l), mma_done (the UMMAs of the stage finished:
-  // frees both the x tile and the TMEM operand). The MMA issuer waits on one
-  // barrier and commits one per k-block: every barrier operation in its loop
-  // delays the next UMMA.
+  // frees both the x tiles and the TMEM operand).
   uint64_t* full_l = bars;
   uint64_t* read_w = bars + NS;
   uint64_t* full_a = bars + 2 * NS;
   uint64_t* mma_done = bars + 3 * NS;
   uint64_t* full_acc = bars + 4 * NS;
   uint64_t* empty_acc = full_acc + 2;
+  uint64_t* recv = full_acc + 4;  // split K: the other ranks' partial columns landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int KS = p.ksplit;
+  const int cpo = (BT / kXChunk) / KS;  // exchanged chunks owned per rank
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -142,7 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       mbar_init(&full_acc[i], 1);
       mbar_init(&empty_acc[i], kEpiWarps);
     }
+    mbar_init(recv, 1);
     fence_barrier_init();
+    if (KS > 1) mbar_arrive_expect_tx(recv, (uint32_t)((KS - 1) * BW * cpo * kXChunk * 4));
   }
   if (warp == kWarpMma) {
     tmem_alloc(tmem_slot, TM::kCols);
@@ -156,7 +179,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   // everything below may read what the previous kernel on the stream wrote
   pdl_wait_prior_grids();
 
-  const int num_units = p.num_w_tiles * p.num_t_tiles;  // token tile fastest
+  // work units: (tile, K range), token tile fastest; a split tile is one cluster
+  const int num_units = p.num_w_tiles * p.num_t_tiles * KS;
+  auto unit_tile = [&](int u, int& wt, int& tt) {
+    const int tile = u / KS;
+    wt = tile / p.num_t_tiles;
+    tt = tile - wt * p.num_t_tiles;
+  };
+  auto unit_kb = [&](int u, int& lo, int& hi) {  // k-blocks [lo, hi) of unit u
+    const int ks = u % KS;
+    lo = (int)(((int64_t)ks * p.num_kb) / KS);
+    hi = (int)(((int64_t)(ks + 1) * p.num_kb) / KS);
+  };
   bool ok = true;
 
   if (warp == kWarpTma) {
@@ -165,17 +199,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       tma_prefetch_desc(&wmap);
       int it = 0;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        const int wt = u / p.num_t_tiles;
-        const int tt = u - wt * p.num_t_tiles;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        int wt, tt, lo, hi;
+        unit_tile(u, wt, tt);
+        unit_kb(u, lo, hi);
+        for (int kb0 = lo; kb0 < hi; kb0 += KPS, ++it) {
           const int s = it % NS;
           const uint32_t ph = ((it / NS) & 1) ^ 1;  // previous use of the stage
           if (!(ok = mbar_wait(&read_w[s], ph, p.status, 50, abort_flag))) break;
           if (!(ok = mbar_wait(&mma_done[s], ph, p.status, 57, abort_flag))) break;
-          mbar_arrive_expect_tx(&full_l[s], L::kXBytes + TsFmt<FMT>::kWcBytes);
-          tma_load_2d(smem + L::kX + s * L::kXBytes, &xmap, &full_l[s], kb * BK, tt * BT);
-          tma_load_2d(smem + L::kWc + s * TsFmt<FMT>::kWcBytes, &wmap, &full_l[s],
-                      FMT == 0 ? kb * (BK / 8) : kb * BK, wt * BW);
+          const int nk = hi - kb0 < KPS ? hi - kb0 : KPS;
+          mbar_arrive_expect_tx(&full_l[s], (uint32_t)nk * (L::kXBytes + TsFmt<FMT>::kWcBytes));
+          for (int i = 0; i < nk; ++i) {
+            const int kb = kb0 + i;
+            tma_load_2d(smem + L::kX + (s * KPS + i) * L::kXBytes, &xmap, &full_l[s], kb * BK, tt * BT);
+            tma_load_2d(smem + L::kWc + (s * KPS + i) * TsFmt<FMT>::kWcBytes, &wmap, &full_l[s],
+                        FMT == 0 ? kb * (BK / 8) : kb * BK, wt * BW);
+          }
         }
       }
       // let in-flight copies land before the CTA can exit
@@ -190,7 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
     if (lane == 0) {
       int it = 0, tcount = 0;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++tcount) {
-        const int tt = u % p.num_t_tiles;
+        int wt, tt, lo, hi;
+        unit_tile(u, wt, tt);
+        unit_kb(u, lo, hi);
         // UMMA N: the tile's tokens rounded up to 16 (the x rows past M are
         // zero-filled by TMA; their accumulator columns are never stored)
         int n_eff = p.M - tt * BT;
@@ -200,16 +241,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         if (!(ok = mbar_wait(&empty_acc[acc], ((tcount >> 1) & 1) ^ 1, p.status, 51, abort_flag))) break;
         tc_fence_after();
         const uint32_t d = tmem_base + TM::kAcc + acc * BT;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int kb0 = lo; kb0 < hi; kb0 += KPS, ++it) {
           const int s = it % NS;
           if (!(ok = mbar_wait(&full_a[s], (it / NS) & 1, p.status, 53, abort_flag))) break;
           tc_fence_after();
-          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kX + s * L::kXBytes));
-          const uint32_t a = tmem_base + TM::kA + s * 32;
+          const int nk = hi - kb0 < KPS ? hi - kb0 : KPS;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            // A: +8 TMEM columns per 16 K; B: +32 bytes inside the swizzled row
-            umma_f16_ts(d, a + 8 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int i = 0; i < KPS; ++i) {
+            if (i < nk) {
+              const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kX + (s * KPS + i) * L::kXBytes));
+              const uint32_t a = tmem_base + TM::kA + (s * KPS + i) * 32;
+#pragma unroll
+              for (int kk = 0; kk < BK / 16; ++kk) {
+                // A: +8 TMEM columns per 16 K; B: +32 bytes inside the swizzled row
+                umma_f16_ts(d, a + 8 * kk, bdesc + 2 * kk, idesc, (kb0 > lo || i > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
           }
           tc_commit(&mma_done[s]);
         }
@@ -220,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   } else if (warp < kWarpEpi0) {
     // ---------------- converters: packed weight -> TMEM operand ----------------
     const int sub = warp & 3;                   // TMEM sub-partition = 32 weight rows
-    const int half = (warp - kWarpConv0) >> 2;  // 32-column half of the k-block
+    const int half = (warp - kWarpConv0) >> 2;  // 32-column half of each k-block
     const int row = sub * 32 + lane;            // weight row within the tile
     const uint32_t a_lane = tmem_base + ((uint32_t)(sub * 32) << 16) + TM::kA + half * 16;
     // AWQ: the (scale, zero) pairs this thread needs, in the order it needs
@@ -228,19 +275,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
     // register ring so their latency hides behind whole groups of k-blocks
     const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
     const unsigned short* zr16 = reinterpret_cast<const unsigned short*>(p.zeros);
-    int pu = blockIdx.x, pg = 0;
+    int pu = blockIdx.x, pg = 0, pg_hi = 0;
+    auto unit_groups = [&](int u, int& glo, int& ghi) {
+      int lo, hi;
+      unit_kb(u, lo, hi);
+      glo = (lo * BK) / p.group_size;
+      ghi = hi > lo ? ((hi - 1) * BK) / p.group_size + 1 : glo;
+    };
+    if (pu < num_units) unit_groups(pu, pg, pg_hi);
     auto load_sz = [&]() -> uint32_t {
       uint32_t v = 0;
+      while (pu < num_units && pg >= pg_hi) {
+        pu += gridDim.x;
+        if (pu < num_units) unit_groups(pu, pg, pg_hi);
+      }
       if (pu < num_units) {
-        const int n = (pu / p.num_t_tiles) * BW + row;
+        int wt, tt;
+        unit_tile(pu, wt, tt);
+        const int n = wt * BW + row;
         if (n < p.N) {
           const int64_t off = (int64_t)n * p.G + pg;
           v = (uint32_t)__ldg(sc16 + off) | ((uint32_t)__ldg(zr16 + off) << 16);
         }
-        if (++pg == p.G) {
-          pg = 0;
-          pu += gridDim.x;
-        }
+        ++pg;
       }
       return v;
     };
@@ -253,28 +310,38 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
     TsRowDq<BF16> rp{};
     int it = 0;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-      for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+      int lo, hi;
+      unit_kb(u, lo, hi);
+      for (int kb0 = lo; kb0 < hi; kb0 += KPS, ++it) {
         const int s = it % NS;
         const uint32_t ph = (it / NS) & 1;
-        if constexpr (FMT == 0) {
-          if ((kb * BK) % p.group_size == 0) {  // a new group (kb = 0 included)
-            rp = ts_row_dq_packed<BF16>(sz0);
-            sz0 = sz1;
-            sz1 = sz2;
-            sz2 = load_sz();
-          }
-        }
         if (!(ok = mbar_wait(&full_l[s], ph, p.status, 54, abort_flag))) break;
-        uint32_t o[16];
-        ts_convert_k32<FMT, BF16>(smem_u32(smem + L::kWc + s * TsFmt<FMT>::kWcBytes), row, half, rp, o);
-        // the packed tile is consumed (the x tile of the stage is freed by
-        // the UMMAs' commit)
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&read_w[s]);
         // the TMEM operand stage is free once the UMMAs of its previous use finished
         if (!(ok = mbar_wait(&mma_done[s], ph ^ 1, p.status, 55, abort_flag))) break;
         tc_fence_after();
-        tmem_st_32x32b_x16(a_lane + s * 32, o);
+        const int nk = hi - kb0 < KPS ? hi - kb0 : KPS;
+#pragma unroll
+        for (int i = 0; i < KPS; ++i) {
+          if (i < nk) {
+            const int kb = kb0 + i;
+            if constexpr (FMT == 0) {
+              if (kb == lo || (kb * BK) % p.group_size == 0) {  // a new group
+                rp = ts_row_dq_packed<BF16>(sz0);
+                sz0 = sz1;
+                sz1 = sz2;
+                sz2 = load_sz();
+              }
+            }
+            uint32_t o[16];
+            ts_convert_k32<FMT, BF16>(smem_u32(smem + L::kWc + (s * KPS + i) * TsFmt<FMT>::kWcBytes), row,
+                                      half, rp, o);
+            tmem_st_32x32b_x16(a_lane + (s * KPS + i) * 32, o);
+          }
+        }
+        // the packed tiles are consumed (the x tiles of the stage are freed by
+        // the UMMAs' commit)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&read_w[s]);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -285,30 +352,101 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
     // ---------------- epilogue: TMEM -> registers -> y ----------------
     const int sub = warp & 3;
     const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
+    const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;
+    uint16_t* y = static_cast<uint16_t*>(p.y);
     int tcount = 0;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++tcount) {
-      const int wt = u / p.num_t_tiles;
-      const int tt = u - wt * p.num_t_tiles;
+      int wt, tt;
+      unit_tile(u, wt, tt);
       const int acc = tcount & 1;
       if (!(ok = mbar_wait(&full_acc[acc], (tcount >> 1) & 1, p.status, 56, abort_flag))) break;
       tc_fence_after();
+      if (KS > 1) break;  // split K: the accumulator stays in TMEM for the exchange below
       const int n = wt * BW + sub * 32 + lane;  // this thread's output feature
-      const float bn =
-          (p.bias_dtype != NSQ_DTYPE_NONE && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
-      const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;
+      const float bn = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
       const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16) + TM::kAcc + acc * BT;
-      uint16_t* y = static_cast<uint16_t*>(p.y);
       const int m0 = tt * BT;
 #pragma unroll 1
       for (int c = 0; c < BT / 32 && m0 + c * 32 < p.M; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(taddr + c * 32, r);
         tmem_ld_wait();
-        ts_store_tokens<BF16>(y, p.M, p.N, n, m0 + c * 32, r, wscale, has_bias, bn, lane);
+        ts_store_tokens<BF16, 32>(y, p.M, p.N, n, m0 + c * 32, r, wscale, has_bias, bn, lane);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_acc[acc]);
+    }
+  }
+
+  if (KS > 1) {
+    // every CTA of the cluster is done with its main loop: all x rings are
+    // free to receive the partial columns
+    __syncwarp();
+    cluster_arrive_rel();
+    cluster_wait_acq();
+    if (warp >= kWarpEpi0 && ok) {
+      const int me = (int)cluster_ctarank();
+      const int sub = warp & 3;
+      const int r_in = sub * 32 + lane;  // this thread's row (output feature) of the tile
+      int wt, tt;
+      unit_tile(blockIdx.x, wt, tt);
+      const uint32_t units = (uint32_t)cpo * 4;  // 16-byte units per slot row
+      const uint32_t slot_bytes = (uint32_t)BW * units * 16;
+      const uint32_t row_off = (uint32_t)r_in * units * 16;
+      const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16);  // accumulator 0
+      const uint32_t rbar = smem_u32(recv);
+      // slot q (the partial of rank q) of an owner: [128 rows][cpo chunks of 16 fp32]
+#pragma unroll 1
+      for (int c = 0; c < BT / kXChunk; ++c) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(taddr + c * kXChunk, r);
+        tmem_ld_wait();
+        const int owner = c / cpo, lc = c - owner * cpo;
+        const uint32_t local = smem_u32(smem + L::kX) + me * slot_bytes + row_off;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t off = ts_slot_unit((uint32_t)(lc * 4 + j), (uint32_t)r_in, units);
+          if (owner == me) {
+            sts128(local + off, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+          } else {
+            st_async_f32x4(dsmem_map(local + off, (uint32_t)owner), __uint_as_float(r[4 * j]),
+                           __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                           __uint_as_float(r[4 * j + 3]), dsmem_map(rbar, (uint32_t)owner));
+          }
+        }
+      }
+      named_bar_sync(3, kEpiWarps * 32);  // this CTA's own slot is written
+      if (mbar_wait(recv, 0, p.status, 58, nullptr)) {
+        const int n = wt * BW + r_in;
+        const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
+        const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;
+        const float bn = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+        const uint32_t base = smem_u32(smem + L::kX) + row_off;
+#pragma unroll 1
+        for (int lc = 0; lc < cpo; ++lc) {
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+          for (int q = 0; q < KS; ++q) {  // rank order: the sum does not depend on timing
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 w =
+                  lds128(base + q * slot_bytes + ts_slot_unit((uint32_t)(lc * 4 + j), (uint32_t)r_in, units));
+              v[4 * j] += __uint_as_float(w.x);
+              v[4 * j + 1] += __uint_as_float(w.y);
+              v[4 * j + 2] += __uint_as_float(w.z);
+              v[4 * j + 3] += __uint_as_float(w.w);
+            }
+          }
+          uint32_t rr[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rr[i] = __float_as_uint(v[i]);
+          ts_store_tokens<BF16, 16>(static_cast<uint16_t*>(p.y), p.M, p.N, n, tt * BT + (me * cpo + lc) * kXChunk,
+                                    rr, wscale, has_bias, bn, lane);
+        }
+      }
+      tc_fence_before();  // the TMEM reads above precede the deallocation
     }
   }
 
@@ -336,8 +474,15 @@ cudaError_t launch_ts(const CUtensorMap& xmap, const CUtensorMap& wmap, const Ts
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   int na = 0;
+  if (p.ksplit > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = p.ksplit;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
   if (pdl_enabled()) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
@@ -349,7 +494,7 @@ cudaError_t launch_ts(const CUtensorMap& xmap, const CUtensorMap& wmap, const Ts
 }
 
 template <int BT>
-int run_ts(const LinearArgs& a, cudaStream_t stream) {
+int run_ts(const LinearArgs& a, int ksplit, cudaStream_t stream) {
   CUtensorMap xmap, wmap;
   CUresult cr = encode_tensor_map_2d(
       &xmap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
@@ -382,9 +527,11 @@ int run_ts(const LinearArgs& a, cudaStream_t stream) {
   p.num_w_tiles = (a.N + BW - 1) / BW;
   p.num_t_tiles = (a.M + BT - 1) / BT;
   p.num_kb = (a.K + BK - 1) / BK;
-  const int units = p.num_w_tiles * p.num_t_tiles;
+  p.ksplit = ksplit;
+  const int tiles = p.num_w_tiles * p.num_t_tiles;
   const int sms = num_sms();
-  const int grid = units < sms ? units : sms;
+  // a split launch runs one tile per cluster; the plan keeps it within one wave
+  const int grid = ksplit > 1 ? tiles * ksplit : (tiles < sms ? tiles : sms);
   cudaError_t e;
   if (a.fmt == 0) {
     e = a.x_bf16 ? launch_ts<0, true, BT>(xmap, wmap, p, grid, stream)
@@ -398,29 +545,42 @@ int run_ts(const LinearArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
-int prefill_ts_tokens_per_tile(int64_t M, int64_t K, int64_t N) {
-  (void)K;
-  // Problems with at most 2^20 outputs (the shared-memory-operand kernels'
-  // 128 x 256 / 256 x 256 tiles leave most SMs idle there): the narrowest
-  // token tile whose units still fit in one wave. Measured on B200 against
-  // those kernels on the Qwen2.5-0.5B shapes (FP8 / AWQ): 1.7-1.9x faster at
-  // M = 128, 1.3x at M = 1024 (q/k/v/o), 1.3x for k/v at M = 8192; slower
-  // for the larger outputs.
-  if (M <= kDecodeMaxM || M * N > ((int64_t)1 << 20)) return 0;
-  const int64_t wt = (N + BW - 1) / BW;
+TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N) {
+  // The one-CTA kernel serves problems that CTA pairs of 256 x 256 tiles
+  // would leave mostly idle: outputs of at most 2^20 elements, or pair tiles
+  // covering less than half of the SMs. The token tile and K split minimise
+  // a cost in k-block times: rounds x (k-blocks per CTA x tile cost + fixed
+  // cost) with a 128-token tile 1.3x a 64-token one and a split paying the
+  // partial-tile exchange; at least 4 k-blocks per CTA.
+  TsPlan best{0, 1};
+  if (M <= kDecodeMaxM) return best;
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
   const int sms = num_sms();
+  if (M * N > ((int64_t)1 << 20) && pair_tiles * 4 > sms) return best;
+  const int64_t kb = (K + BK - 1) / BK;
+  const int64_t wt = (N + BW - 1) / BW;
+  double best_cost = 0.0;
   for (int bt : {64, 128}) {
-    if (wt * ((M + bt - 1) / bt) <= sms) return bt;
+    const int64_t units = wt * ((M + bt - 1) / bt);
+    for (int ks = 1; ks <= bt / kXChunk; ks *= 2) {
+      if (ks > 1 && (units * ks > sms || kb < 4 * ks)) break;
+      const int64_t rounds = (units * ks + sms - 1) / sms;
+      const double per_kb = bt == 128 ? 1.3 : 1.0;
+      const double cost = (double)rounds * ((double)((kb + ks - 1) / ks) * per_kb + 10.0 + (ks > 1 ? 6.0 : 0.0));
+      if (best.tokens_per_tile == 0 || cost < best_cost) {
+        best = TsPlan{bt, ks};
+        best_cost = cost;
+      }
+    }
   }
-  return 192;
+  return best;
 }
 
-int run_prefill_ts_linear(const LinearArgs& a, int tokens_per_tile, cudaStream_t stream) {
+int run_prefill_ts_linear(const LinearArgs& a, TsPlan plan, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0) return NSQ_OK;
-  switch (tokens_per_tile) {
-    case 64: return run_ts<64>(a, stream);
-    case 128: return run_ts<128>(a, stream);
-    case 192: return run_ts<192>(a, stream);
+  switch (plan.tokens_per_tile) {
+    case 64: return run_ts<64>(a, plan.ksplit, stream);
+    case 128: return run_ts<128>(a, plan.ksplit, stream);
     default: return NSQ_ENOTSUP;
   }
 }

@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
           uint32_t r[32];
           tmem_ld_32x32b_x32(taddr + c * 32, r);
           tmem_ld_wait();
-          ts_store_tokens<BF16>(y, p.M, p.N, n, m0 + c * 32, r, wscale, has_bias, bn, lane);
+          ts_store_tokens<BF16, 32>(y, p.M, p.N, n, m0 + c * 32, r, wscale, has_bias, bn, lane);
         }
         tc_fence_before();
         __syncwarp();

@@ -107,17 +107,17 @@ __device__ __forceinline__ void ts_convert_k32(uint32_t tile, int row, int half,
   }
 }
 
-// Scale, bias, round and store 32 tokens m0 .. m0+31 of output feature n held
-// by this lane (accumulator chunk r). With N even, lanes 2i and 2i+1 (features
-// n, n+1) exchange values so the even lane stores the pair of token 2j and the
-// odd lane the pair of token 2j+1 (one 32-bit store each).
-template <bool BF16>
-__device__ __forceinline__ void ts_store_tokens(uint16_t* y, int M, int N, int n, int m0, const uint32_t (&r)[32],
+// Scale, bias, round and store T tokens m0 .. m0+T-1 of output feature n held
+// by this lane (accumulator chunk r, fp32 bits). With N even, lanes 2i and
+// 2i+1 (features n, n+1) exchange values so the even lane stores the pair of
+// token 2j and the odd lane the pair of token 2j+1 (one 32-bit store each).
+template <bool BF16, int T>
+__device__ __forceinline__ void ts_store_tokens(uint16_t* y, int M, int N, int n, int m0, const uint32_t (&r)[T],
                                                 float wscale, bool has_bias, float bn, int lane) {
   if ((N & 1) == 0) {
     const bool odd = lane & 1;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < T / 2; ++j) {
       const float a0 = __uint_as_float(r[2 * j]), a1 = __uint_as_float(r[2 * j + 1]);
       const float v0 = has_bias ? fmaf(a0, wscale, bn) : a0 * wscale;
       const float v1 = has_bias ? fmaf(a1, wscale, bn) : a1 * wscale;
@@ -131,7 +131,7 @@ __device__ __forceinline__ void ts_store_tokens(uint16_t* y, int M, int N, int n
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < T; ++j) {
       const float a = __uint_as_float(r[j]);
       const float v = has_bias ? fmaf(a, wscale, bn) : a * wscale;
       const int m = m0 + j;
