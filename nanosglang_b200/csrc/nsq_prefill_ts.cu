@@ -527,11 +527,12 @@ int run_ts(const LinearArgs& a, int ksplit, cudaStream_t stream) {
   p.num_w_tiles = (a.N + BW - 1) / BW;
   p.num_t_tiles = (a.M + BT - 1) / BT;
   p.num_kb = (a.K + BK - 1) / BK;
-  p.ksplit = ksplit;
+  // every rank of a split needs a non-empty K range
+  p.ksplit = ksplit > 1 && ksplit <= p.num_kb && (BT / kXChunk) % ksplit == 0 ? ksplit : 1;
   const int tiles = p.num_w_tiles * p.num_t_tiles;
   const int sms = num_sms();
   // a split launch runs one tile per cluster; the plan keeps it within one wave
-  const int grid = ksplit > 1 ? tiles * ksplit : (tiles < sms ? tiles : sms);
+  const int grid = p.ksplit > 1 ? tiles * p.ksplit : (tiles < sms ? tiles : sms);
   cudaError_t e;
   if (a.fmt == 0) {
     e = a.x_bf16 ? launch_ts<0, true, BT>(xmap, wmap, p, grid, stream)
@@ -548,10 +549,12 @@ int run_ts(const LinearArgs& a, int ksplit, cudaStream_t stream) {
 TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N) {
   // The one-CTA kernel serves problems that CTA pairs of 256 x 256 tiles
   // would leave mostly idle: outputs of at most 2^20 elements, or pair tiles
-  // covering less than half of the SMs. The token tile and K split minimise
-  // a cost in k-block times: rounds x (k-blocks per CTA x tile cost + fixed
-  // cost) with a 128-token tile 1.3x a 64-token one and a split paying the
-  // partial-tile exchange; at least 4 k-blocks per CTA.
+  // covering less than a quarter of the SMs. The token tile and K split
+  // minimise rounds x (k-blocks per CTA x 0.28 + 5.7 + exchange) us, the
+  // exchange of a split costing ~1 us for 64-token tiles and 2.5 + 0.3 ks us
+  // for 128-token tiles -- a fit of forced plans timed on B200 over the
+  // Qwen2.5-0.5B and Llama-3-8B shapes at M = 128 / 1024 (FP8 and AWQ alike
+  // to within a few percent of their best plan). At least 2 k-blocks per CTA.
   TsPlan best{0, 1};
   if (M <= kDecodeMaxM) return best;
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
@@ -563,10 +566,10 @@ TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N) {
   for (int bt : {64, 128}) {
     const int64_t units = wt * ((M + bt - 1) / bt);
     for (int ks = 1; ks <= bt / kXChunk; ks *= 2) {
-      if (ks > 1 && (units * ks > sms || kb < 4 * ks)) break;
+      if (ks > 1 && (units * ks > sms || (kb + ks - 1) / ks < 2)) break;
       const int64_t rounds = (units * ks + sms - 1) / sms;
-      const double per_kb = bt == 128 ? 1.3 : 1.0;
-      const double cost = (double)rounds * ((double)((kb + ks - 1) / ks) * per_kb + 10.0 + (ks > 1 ? 6.0 : 0.0));
+      const double exchange = ks == 1 ? 0.0 : (bt == 64 ? 1.0 : 2.5 + 0.3 * ks);
+      const double cost = (double)rounds * ((double)((kb + ks - 1) / ks) * 0.28 + 5.7 + exchange);
       if (best.tokens_per_tile == 0 || cost < best_cost) {
         best = TsPlan{bt, ks};
         best_cost = cost;
