@@ -14,20 +14,19 @@
 // 512 cycles of MMA), and the conversion of a weight row is shared by 256
 // tokens.
 //
-// Warp roles (both CTAs, 608 threads each):
+// Warp roles (both CTAs, 576 threads each):
 //   warp 0        TMA producer: x tile [128 tokens x 64] (128-byte swizzle)
 //                 and this CTA's packed weight tile [128 rows x 64 columns],
 //                 KPS of each per stage, NS-stage ring, completion on this
 //                 CTA's own barrier.
 //   warp 1        TMEM allocation (512 columns, paired); in the even CTA, lane
 //                 0 issues the UMMAs and the multicast commits.
-//   warp 2        forwarder: once this CTA's converters finished a stage, one
-//                 arrival on the even CTA's operand barrier (a single
-//                 cluster-scope arrival per CTA and stage).
-//   warps 3..10   converters: warp w serves TMEM sub-partition w % 4 (32
-//                 weight rows, one per lane) and half (w - 3) / 4 of the 64
-//                 columns; tcgen05.st into an NS-stage TMEM operand ring.
-//   warps 11..18  epilogue: two warps per TMEM sub-partition (128 tokens
+//   warps 2..9    converters: warp w serves TMEM sub-partition w % 4 (32
+//                 weight rows, one per lane) and half (w - 2) / 4 of the 64
+//                 columns; tcgen05.st into an NS-stage TMEM operand ring, then
+//                 each warp arrives on the even CTA's operand barrier (a hop
+//                 through one forwarding warp per CTA measured ~5% slower).
+//   warps 10..17  epilogue: two warps per TMEM sub-partition (128 tokens
 //                 each), tcgen05.ld of the accumulator (lane = output feature,
 //                 column = token), scale (FP8), bias, rounding into a staged
 //                 [tokens][features] tile, TMA stores of y.
@@ -53,8 +52,7 @@ constexpr int BK = 64;
 constexpr int KPS = 2;    // k-blocks per stage: one barrier round per 8 UMMAs
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
-constexpr int kWarpFwd = 2;
-constexpr int kWarpConv0 = 3;
+constexpr int kWarpConv0 = 2;
 constexpr int kConvWarps = 8;
 constexpr int kWarpEpi0 = kWarpConv0 + kConvWarps;
 constexpr int kEpiWarps = 8;
@@ -77,8 +75,8 @@ struct Ts2Smem {
   static constexpr int kY = kWc + NS * KPS * kWcBytes;  // staged y tile: 2 x [256 tokens][64 features]
   static constexpr int kYHalfBytes = BTP * 64 * 2;
   static constexpr int kBar = kY + (STAGED ? 2 * kYHalfBytes : 0);
-  // full_l[NS], read_w[NS], conv_done[NS], full_a[NS], mma_done[NS], full_acc, empty_acc
-  static constexpr int kNumBars = 5 * NS + 2;
+  // full_l[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc, empty_acc
+  static constexpr int kNumBars = 4 * NS + 2;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kTotal = kAbort + 4;
@@ -119,15 +117,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   // Per stage s (both CTAs unless noted): full_l (this CTA's x and packed
   // weight bytes), read_w (this CTA's converters read the packed weight),
-  // conv_done (this CTA's converters wrote its TMEM operand; implies full_l),
-  // full_a (even CTA: one arrival per CTA's forwarder), mma_done (multicast
-  // commit: frees the x tile and the TMEM operand in both CTAs).
+  // full_a (even CTA: every converter warp of both CTAs wrote its part of the
+  // TMEM operand; each waited for its CTA's full_l first, so full_a implies
+  // both x tiles landed), mma_done (multicast commit: frees the x tile and
+  // the TMEM operand in both CTAs).
   uint64_t* full_l = bars;
   uint64_t* read_w = bars + NS;
-  uint64_t* conv_done = bars + 2 * NS;
-  uint64_t* full_a = bars + 3 * NS;
-  uint64_t* mma_done = bars + 4 * NS;
-  uint64_t* full_acc = bars + 5 * NS;
+  uint64_t* full_a = bars + 2 * NS;
+  uint64_t* mma_done = bars + 3 * NS;
+  uint64_t* full_acc = bars + 4 * NS;
   uint64_t* empty_acc = full_acc + 1;  // even CTA: every epilogue warp of both CTAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
@@ -144,8 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full_l[i], 1);
       mbar_init(&read_w[i], kConvWarps);
-      mbar_init(&conv_done[i], kConvWarps);
-      mbar_init(&full_a[i], 2);
+      mbar_init(&full_a[i], 2 * kConvWarps);
       mbar_init(&mma_done[i], 1);
     }
     mbar_init(full_acc, 1);
@@ -229,22 +226,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
         tc_commit_pair_mc(full_acc, 0x3);
       }
     }
-  } else if (warp == kWarpFwd) {
-    if (lane == 0) {
-      const uint32_t full_a_leader0 = dsmem_map(smem_u32(&full_a[0]), 0);
-      const int total = ((num_units - cid + ncl - 1) / ncl) * p.num_st;
-      for (int it = 0; it < total; ++it) {
-        const int s = it % NS;
-        if (!(ok = mbar_wait(&conv_done[s], (it / NS) & 1, p.status, 154, abort_flag))) break;
-        mbar_arrive_cluster(full_a_leader0 + s * 8);
-      }
-    }
   } else if (warp < kWarpEpi0) {
     // ---------------- converters: packed weight -> TMEM operand ----------------
     const int sub = warp & 3;                   // TMEM sub-partition = 32 weight rows
     const int half = (warp - kWarpConv0) >> 2;  // 32-column half of the k-block
     const int row = sub * 32 + lane;            // weight row within this CTA's 128
     const uint32_t a_lane = tmem_base + ((uint32_t)(sub * 32) << 16) + kTmemA + half * 16;
+    const uint32_t full_a_leader0 = dsmem_map(smem_u32(&full_a[0]), 0);
     // AWQ: (scale, zero) of this thread's row, in the order of use, loaded
     // three groups ahead into a register ring
     const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
@@ -303,16 +291,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&conv_done[s]);
+        if (lane == 0) mbar_arrive_cluster(full_a_leader0 + s * 8);
       }
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> staged tile -> TMA store ----------------
     // STAGED: the accumulator is drained into shared memory (bf16/fp16, two
     // 128-byte-swizzled [256 tokens][64 features] halves) and released at
-    // once; the TMA stores of the tile overlap the next tile's UMMAs. Else the
-    // lanes store y directly (long K, where a deeper ring is worth more, or
-    // N % 8 != 0: no 16-byte row pitch for a tensor map).
+    // once; the TMA stores of the tile overlap the next tile's UMMAs. The
+    // drain reads TMEM in the 16x256b shape (the m8n8 fragment layout) and
+    // writes 8 tokens x 8 features per stmatrix.trans, so the transpose costs
+    // no shuffles. Else the lanes store y directly (long K, where a deeper
+    // ring is worth more, or N % 8 != 0: no 16-byte row pitch for a tensor map).
     const int sub = warp & 3;
     const int chalf = (warp - kWarpEpi0) >> 2;  // tokens [128 chalf, 128 chalf + 128) of the tile
     const int etid = threadIdx.x - kWarpEpi0 * 32;
@@ -320,12 +310,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
     const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;
     const uint32_t empty_acc_leader = dsmem_map(smem_u32(empty_acc), 0);
     uint16_t* y = static_cast<uint16_t*>(p.y);
-    // staged position of this lane's feature: half (sub / 2), 16-byte chunk and byte in the row
-    const int fl = (sub & 1) * 32 + lane;
+    // staged tile half of this warp's 32 features (sub / 2); stmatrix row
+    // addresses: thread 8q + i writes row i (a token) of matrix q (features
+    // 8q .. 8q+7 of the warp) = 16-byte chunk (sub & 1) * 4 + q of the row
     const uint32_t ystage = smem_u32(smem + L::kY + (sub >> 1) * L::kYHalfBytes);
-    const uint32_t ychunk = (uint32_t)(fl >> 3);
-    const uint32_t ybyte = (uint32_t)((fl & 6) * 2);  // the pair (f & ~1, f | 1) starts here
-    const bool odd = lane & 1;
+    const uint32_t ychunk = (uint32_t)((sub & 1) * 4 + (lane >> 3));
+    const int g = lane >> 2;  // fragment row: features g, g + 8 of each 16-lane half
     int tcount = 0;
     for (int u = cid; u < num_units && ok; u += ncl, ++tcount) {
       const int wt = u / p.num_t_tiles;
@@ -336,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
         break;
       }
       tc_fence_after();
-      const int n = wt * (2 * BWC) + (int)rank * BWC + sub * 32 + lane;  // this thread's output feature
+      const int n = wt * (2 * BWC) + (int)rank * BWC + sub * 32 + lane;  // this lane's output feature
       const float bn = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
       const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16) + chalf * 128;
       const int m0 = tt * BTP + chalf * 128;  // accumulator column c holds token tt * 256 + c
@@ -344,26 +334,32 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
         // the previous tile's stores have read the staged tile
         if (etid == 0) bulk_wait_group_read<0>();
         named_bar_sync(1, kEpiWarps * 32);
+        // bias of the fragment rows this thread holds: features 16h + g (+ 8)
+        float bf[4] = {0.f, 0.f, 0.f, 0.f};
+        if (has_bias) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int nq = wt * (2 * BWC) + (int)rank * BWC + sub * 32 + 8 * q + g;
+            bf[q] = nq < p.N ? load_bias(p.bias, p.bias_dtype, nq) : 0.f;
+          }
+        }
 #pragma unroll 1
         for (int c = 0; c < 4 && m0 + c * 32 < p.M; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          // the accumulator's 32 lanes of this warp as two 16-lane fragment
+          // halves, 32 token columns, then 4 transposed 8x8 stores per 8 tokens
+          uint32_t r0[16], r1[16];
+          tmem_ld_16x256b_x4(taddr + c * 32, r0);
+          tmem_ld_16x256b_x4(taddr + (16u << 16) + c * 32, r1);
           tmem_ld_wait();
-          // lanes 2i, 2i+1 (features f, f+1) exchange values: the even lane
-          // stages the pair of token a, the odd lane that of token a + 4
-          // (rows 4 apart fall on different chunk swizzles: no bank conflicts)
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int a = (j >> 2) * 8 + (j & 3);
-            const float va = has_bias ? fmaf(__uint_as_float(r[a]), wscale, bn) : __uint_as_float(r[a]) * wscale;
-            const float vb =
-                has_bias ? fmaf(__uint_as_float(r[a + 4]), wscale, bn) : __uint_as_float(r[a + 4]) * wscale;
-            const float recv = __shfl_xor_sync(0xffffffffu, odd ? va : vb, 1);
-            const uint32_t t = (uint32_t)(chalf * 128 + c * 32 + a + (odd ? 4 : 0));  // staged row
-            const uint32_t w = odd ? ts_pack2<BF16>(recv, vb) : ts_pack2<BF16>(va, recv);
-            asm volatile("st.shared.b32 [%0], %1;" ::"r"(ystage + t * 128 + ((ychunk ^ (t & 7)) << 4) + ybyte),
-                         "r"(w)
-                         : "memory");
+          for (int j = 0; j < 4; ++j) {
+            auto v = [&](uint32_t x, float b) { return has_bias ? fmaf(__uint_as_float(x), wscale, b) : __uint_as_float(x) * wscale; };
+            const uint32_t m0w = ts_pack2<BF16>(v(r0[4 * j], bf[0]), v(r0[4 * j + 1], bf[0]));
+            const uint32_t m1w = ts_pack2<BF16>(v(r0[4 * j + 2], bf[1]), v(r0[4 * j + 3], bf[1]));
+            const uint32_t m2w = ts_pack2<BF16>(v(r1[4 * j], bf[2]), v(r1[4 * j + 1], bf[2]));
+            const uint32_t m3w = ts_pack2<BF16>(v(r1[4 * j + 2], bf[3]), v(r1[4 * j + 3], bf[3]));
+            const uint32_t t = (uint32_t)(chalf * 128 + c * 32 + 8 * j + (lane & 7));  // staged row (token)
+            stmatrix_x4_trans(ystage + t * 128 + ((ychunk ^ (t & 7)) << 4), m0w, m1w, m2w, m3w);
           }
         }
         tc_fence_before();
