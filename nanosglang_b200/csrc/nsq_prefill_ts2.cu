@@ -61,19 +61,24 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = BTP;  // operand stages start after the accumulator
 constexpr int kXBytes = (BTP / 2) * BK * 2;  // one k-block of x: 16 KB per CTA
 
-// Stages (x + packed weight in shared memory, operand in TMEM): 4, or 3 for
-// FP8 when the staged y tile (64 KB) has to fit beside them.
-__host__ __device__ constexpr int ts2_stages(int fmt, bool staged) { return (fmt == 1 && staged) ? 3 : 4; }
+// Stages (x + packed weight in shared memory, operand in TMEM): 4. The staged
+// y tile holds all 256 tokens of a tile (AWQ, 64 KB) or 128 of them (FP8,
+// 32 KB, drained in two rounds), so that 4 stages fit beside it: with 3 the
+// refill of a stage (TMA, conversion, arrival: ~2.5 k cycles) outruns the
+// ring at every tile start.
+constexpr int NS = 4;
+__host__ __device__ constexpr int ts2_stage_rounds(int fmt) { return fmt == 1 ? 2 : 1; }
 
 template <int FMT, bool STAGED>
 struct Ts2Smem {
-  static constexpr int NS = ts2_stages(FMT, STAGED);
+  static constexpr int kRounds = ts2_stage_rounds(FMT);
+  static constexpr int kTokRound = BTP / kRounds;  // tokens staged per round
   static_assert(kTmemA + NS * KPS * 32 <= kTmemCols, "tensor memory budget");
   static constexpr int kWcBytes = FMT == 0 ? BWC * BK / 2 : BWC * BK;
   static constexpr int kX = 0;                          // [NS][KPS] x tiles
   static constexpr int kWc = kX + NS * KPS * kXBytes;   // [NS][KPS] packed weight tiles
   static constexpr int kY = kWc + NS * KPS * kWcBytes;  // staged y tile: 2 x [256 tokens][64 features]
-  static constexpr int kYHalfBytes = BTP * 64 * 2;
+  static constexpr int kYHalfBytes = kTokRound * 64 * 2;
   static constexpr int kBar = kY + (STAGED ? 2 * kYHalfBytes : 0);
   // full_l[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc, empty_acc
   static constexpr int kNumBars = 4 * NS + 2;
@@ -111,7 +116,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
     const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
     const __grid_constant__ CUtensorMap ymap, const Ts2Params p) {
   using L = Ts2Smem<FMT, STAGED>;
-  constexpr int NS = L::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
@@ -297,14 +301,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
   } else {
     // ---------------- epilogue: TMEM -> registers -> staged tile -> TMA store ----------------
     // STAGED: the accumulator is drained into shared memory (bf16/fp16, two
-    // 128-byte-swizzled [256 tokens][64 features] halves) and released at
-    // once; the TMA stores of the tile overlap the next tile's UMMAs. The
-    // drain reads TMEM in the 16x256b shape (the m8n8 fragment layout) and
-    // writes 8 tokens x 8 features per stmatrix.trans, so the transpose costs
-    // no shuffles. Else the lanes store y directly (long K, where a deeper
-    // ring is worth more, or N % 8 != 0: no 16-byte row pitch for a tensor map).
+    // 128-byte-swizzled [tokens][64 features] halves; all 256 tokens at once,
+    // or 128 per round for FP8) and released as soon as the last round is in
+    // shared memory; the TMA stores overlap the next tile's UMMAs. The drain
+    // reads TMEM in the 16x256b shape (the m8n8 fragment layout) and writes 8
+    // tokens x 8 features per stmatrix.trans, so the transpose costs no
+    // shuffles. Else (N % 8 != 0: no 16-byte row pitch for a tensor map) the
+    // lanes store y directly.
     const int sub = warp & 3;
-    const int chalf = (warp - kWarpEpi0) >> 2;  // tokens [128 chalf, 128 chalf + 128) of the tile
+    const int chalf = (warp - kWarpEpi0) >> 2;  // which half of the tokens (of a round) this warp drains
     const int etid = threadIdx.x - kWarpEpi0 * 32;
     const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
     const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;
@@ -331,9 +336,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
       const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16) + chalf * 128;
       const int m0 = tt * BTP + chalf * 128;  // accumulator column c holds token tt * 256 + c
       if constexpr (STAGED) {
-        // the previous tile's stores have read the staged tile
-        if (etid == 0) bulk_wait_group_read<0>();
-        named_bar_sync(1, kEpiWarps * 32);
         // bias of the fragment rows this thread holds: features 16h + g (+ 8)
         float bf[4] = {0.f, 0.f, 0.f, 0.f};
         if (has_bias) {
@@ -343,36 +345,50 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
             bf[q] = nq < p.N ? load_bias(p.bias, p.bias_dtype, nq) : 0.f;
           }
         }
+        // rounds of kTokRound tokens; this warp drains kTokRound / 2 of them
+        constexpr int kWarpTok = L::kTokRound / 2;
 #pragma unroll 1
-        for (int c = 0; c < 4 && m0 + c * 32 < p.M; ++c) {
-          // the accumulator's 32 lanes of this warp as two 16-lane fragment
-          // halves, 32 token columns, then 4 transposed 8x8 stores per 8 tokens
-          uint32_t r0[16], r1[16];
-          tmem_ld_16x256b_x4(taddr + c * 32, r0);
-          tmem_ld_16x256b_x4(taddr + (16u << 16) + c * 32, r1);
-          tmem_ld_wait();
+        for (int rd = 0; rd < L::kRounds; ++rd) {
+          // the previous stores have read the staged tile
+          if (etid == 0) bulk_wait_group_read<0>();
+          named_bar_sync(1, kEpiWarps * 32);
+          const int col0 = rd * L::kTokRound + chalf * kWarpTok;  // accumulator column = token in the tile
+#pragma unroll 1
+          for (int c = 0; c < kWarpTok / 32 && tt * BTP + col0 + c * 32 < p.M; ++c) {
+            // the accumulator's 32 lanes of this warp as two 16-lane fragment
+            // halves, 32 token columns, then 4 transposed 8x8 stores per 8 tokens
+            uint32_t r0[16], r1[16];
+            const uint32_t tcol = tmem_base + ((uint32_t)(sub * 32) << 16) + col0 + c * 32;
+            tmem_ld_16x256b_x4(tcol, r0);
+            tmem_ld_16x256b_x4(tcol + (16u << 16), r1);
+            tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            auto v = [&](uint32_t x, float b) { return has_bias ? fmaf(__uint_as_float(x), wscale, b) : __uint_as_float(x) * wscale; };
-            const uint32_t m0w = ts_pack2<BF16>(v(r0[4 * j], bf[0]), v(r0[4 * j + 1], bf[0]));
-            const uint32_t m1w = ts_pack2<BF16>(v(r0[4 * j + 2], bf[1]), v(r0[4 * j + 3], bf[1]));
-            const uint32_t m2w = ts_pack2<BF16>(v(r1[4 * j], bf[2]), v(r1[4 * j + 1], bf[2]));
-            const uint32_t m3w = ts_pack2<BF16>(v(r1[4 * j + 2], bf[3]), v(r1[4 * j + 3], bf[3]));
-            const uint32_t t = (uint32_t)(chalf * 128 + c * 32 + 8 * j + (lane & 7));  // staged row (token)
-            stmatrix_x4_trans(ystage + t * 128 + ((ychunk ^ (t & 7)) << 4), m0w, m1w, m2w, m3w);
+            for (int j = 0; j < 4; ++j) {
+              auto v = [&](uint32_t x, float b) {
+                return has_bias ? fmaf(__uint_as_float(x), wscale, b) : __uint_as_float(x) * wscale;
+              };
+              const uint32_t m0w = ts_pack2<BF16>(v(r0[4 * j], bf[0]), v(r0[4 * j + 1], bf[0]));
+              const uint32_t m1w = ts_pack2<BF16>(v(r0[4 * j + 2], bf[1]), v(r0[4 * j + 3], bf[1]));
+              const uint32_t m2w = ts_pack2<BF16>(v(r1[4 * j], bf[2]), v(r1[4 * j + 1], bf[2]));
+              const uint32_t m3w = ts_pack2<BF16>(v(r1[4 * j + 2], bf[3]), v(r1[4 * j + 3], bf[3]));
+              const uint32_t t = (uint32_t)(chalf * kWarpTok + c * 32 + 8 * j + (lane & 7));  // staged row
+              stmatrix_x4_trans(ystage + t * 128 + ((ychunk ^ (t & 7)) << 4), m0w, m1w, m2w, m3w);
+            }
           }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(empty_acc_leader);  // the accumulator is free
-        fence_proxy_async_smem();
-        named_bar_sync(1, kEpiWarps * 32);
-        if (etid == 0) {
-          for (int h = 0; h < 2; ++h) {
-            const int f0 = wt * (2 * BWC) + (int)rank * BWC + h * 64;
-            if (f0 < p.N) tma_store_2d(&ymap, smem + L::kY + h * L::kYHalfBytes, f0, tt * BTP);
+          if (rd == L::kRounds - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(empty_acc_leader);  // the accumulator is free
           }
-          bulk_commit_group();
+          fence_proxy_async_smem();
+          named_bar_sync(1, kEpiWarps * 32);
+          if (etid == 0) {
+            for (int h = 0; h < 2; ++h) {
+              const int f0 = wt * (2 * BWC) + (int)rank * BWC + h * 64;
+              if (f0 < p.N) tma_store_2d(&ymap, smem + L::kY + h * L::kYHalfBytes, f0, tt * BTP + rd * L::kTokRound);
+            }
+            bulk_commit_group();
+          }
         }
       } else {
 #pragma unroll 1
@@ -453,17 +469,15 @@ int run_prefill_ts2_linear(const LinearArgs& a, cudaStream_t stream) {
                               CU_TENSOR_MAP_SWIZZLE_64B);
   }
   if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
-  // y: [M][N] in the activation dtype, stored as [256 tokens][64 features]
-  // boxes from the staged tile when N % 8 == 0 and the tiles are short in K
-  // (measured on B200: the staged epilogue pays for its smaller ring below
-  // ~16 stages per tile for FP8; AWQ keeps 4 stages either way)
+  // y: [M][N] in the activation dtype, stored as [tokens][64 features] boxes
+  // from the staged tile when N % 8 == 0 (16-byte row pitch for the tensor map)
   CUtensorMap ymap = xmap;
   const int num_st = ((a.K + BK - 1) / BK + KPS - 1) / KPS;
-  const bool staged = (a.N % 8) == 0 && (a.fmt == 0 || num_st < 16);
+  const bool staged = (a.N % 8) == 0;
   if (staged) {
     cr = encode_tensor_map_2d(&ymap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                              a.y, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.N * 2, 64, BTP,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
+                              a.y, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.N * 2, 64,
+                              (uint32_t)(BTP / ts2_stage_rounds(a.fmt)), CU_TENSOR_MAP_SWIZZLE_128B);
     if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
   }
   Ts2Params p{};
