@@ -353,15 +353,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
           if (etid == 0) bulk_wait_group_read<0>();
           named_bar_sync(1, kEpiWarps * 32);
           const int col0 = rd * L::kTokRound + chalf * kWarpTok;  // accumulator column = token in the tile
-#pragma unroll 1
-          for (int c = 0; c < kWarpTok / 32 && tt * BTP + col0 + c * 32 < p.M; ++c) {
-            // the accumulator's 32 lanes of this warp as two 16-lane fragment
-            // halves, 32 token columns, then 4 transposed 8x8 stores per 8 tokens
-            uint32_t r0[16], r1[16];
-            const uint32_t tcol = tmem_base + ((uint32_t)(sub * 32) << 16) + col0 + c * 32;
-            tmem_ld_16x256b_x4(tcol, r0);
-            tmem_ld_16x256b_x4(tcol + (16u << 16), r1);
-            tmem_ld_wait();
+          // two 32-token chunks per TMEM wait (tcgen05.wait::ld waits for every
+          // load in flight, so batching, not prefetching, hides its latency)
+          auto stage_chunk = [&](const uint32_t (&r0)[16], const uint32_t (&r1)[16], int c) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               auto v = [&](uint32_t x, float b) {
@@ -374,6 +368,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
               const uint32_t t = (uint32_t)(chalf * kWarpTok + c * 32 + 8 * j + (lane & 7));  // staged row
               stmatrix_x4_trans(ystage + t * 128 + ((ychunk ^ (t & 7)) << 4), m0w, m1w, m2w, m3w);
             }
+          };
+          const int nc_all = kWarpTok / 32;
+          int nc = (p.M - (tt * BTP + col0) + 31) / 32;
+          nc = nc < nc_all ? nc : nc_all;
+#pragma unroll 1
+          for (int c = 0; c < nc; c += 2) {
+            // the accumulator's 32 lanes of this warp as two 16-lane fragment
+            // halves, 32 token columns each chunk, then 4 transposed 8x8
+            // stores per 8 tokens
+            uint32_t a0[16], a1[16], b0[16], b1[16];
+            const uint32_t tcol = tmem_base + ((uint32_t)(sub * 32) << 16) + col0 + c * 32;
+            tmem_ld_16x256b_x4(tcol, a0);
+            tmem_ld_16x256b_x4(tcol + (16u << 16), a1);
+            if (c + 1 < nc) {
+              tmem_ld_16x256b_x4(tcol + 32, b0);
+              tmem_ld_16x256b_x4(tcol + (16u << 16) + 32, b1);
+            }
+            tmem_ld_wait();
+            stage_chunk(a0, a1, c);
+            if (c + 1 < nc) stage_chunk(b0, b1, c + 1);
           }
           if (rd == L::kRounds - 1) {
             tc_fence_before();
