@@ -395,6 +395,36 @@ def test_linears_capture_in_cuda_graph():
         assert torch.equal(e, o)
 
 
+@pytest.mark.parametrize("m,k,n", [(128, 4864, 896), (1024, 4864, 896), (300, 1024, 1000)])
+def test_split_k_results_do_not_depend_on_timing(m, k, n):
+    """Shapes whose K range is split over a thread-block cluster (the partial
+    columns are exchanged through DSMEM and summed in rank order): repeated
+    eager calls and CUDA-graph replays give bit-identical outputs."""
+    from nanosglang_b200.quantization import AWQLinear, FP8Linear
+    torch.manual_seed(m + n)
+    lin = nn.Linear(k, n, bias=True).cuda().to(torch.bfloat16)
+    mods = (AWQLinear.from_linear(lin, 128), FP8Linear.from_linear(lin))
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    first = [mod(x) for mod in mods]
+    for _ in range(3):
+        for mod, f in zip(mods, first):
+            assert torch.equal(mod(x), f)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for mod in mods:
+            mod(x)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        outs = [mod(x) for mod in mods]
+    for _ in range(2):
+        g.replay()
+        torch.cuda.synchronize()
+        for o, f in zip(outs, first):
+            assert torch.equal(o, f)
+
+
 def test_quantize_model_on_cuda():
     from nanosglang_b200.quantization import AWQLinear, FP8Linear, quantize_model
     for method, cls in (("awq", AWQLinear), ("fp8", FP8Linear)):
