@@ -203,7 +203,7 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
   // Prefill: the weight tile dequantised into tensor memory -- one CTA per
   // 128 rows (K split over a cluster when the tiles are few) for problems
   // that 256 x 256 pair tiles would leave mostly idle, CTA pairs otherwise.
-  const TsPlan tp = prefill_ts_plan(a.M, a.K, a.N);
+  const TsPlan tp = prefill_ts_plan(a.fmt, a.M, a.K, a.N);
   if (tp.tokens_per_tile > 0) return run_prefill_ts_linear(a, tp, stream);
   return run_prefill_ts2_linear(a, stream);
 }

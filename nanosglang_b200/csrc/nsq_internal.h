@@ -60,7 +60,7 @@ struct TsPlan {
   int tokens_per_tile;  // 64 or 128; 0: use the paired kernel
   int ksplit;           // CTAs per tile along K (cluster size)
 };
-TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N);
+TsPlan prefill_ts_plan(int fmt, int64_t M, int64_t K, int64_t N);  // fmt: 0 AWQ, 1 FP8
 int run_prefill_ts_linear(const LinearArgs& a, TsPlan plan, cudaStream_t stream);
 int run_prefill_ts2_linear(const LinearArgs& a, cudaStream_t stream);
 

@@ -546,15 +546,18 @@ int run_ts(const LinearArgs& a, int ksplit, cudaStream_t stream) {
 
 }  // namespace
 
-TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N) {
+TsPlan prefill_ts_plan(int fmt, int64_t M, int64_t K, int64_t N) {
   // The one-CTA kernel serves problems that CTA pairs of 256 x 256 tiles
   // would leave mostly idle: outputs of at most 2^20 elements, or pair tiles
   // covering less than a quarter of the SMs. The token tile and K split
-  // minimise rounds x (k-blocks per CTA x 0.28 + 5.7 + exchange) us, the
-  // exchange of a split costing ~1 us for 64-token tiles and 2.5 + 0.3 ks us
-  // for 128-token tiles -- a fit of forced plans timed on B200 over the
-  // Qwen2.5-0.5B and Llama-3-8B shapes at M = 128 / 1024 (FP8 and AWQ alike
-  // to within a few percent of their best plan). At least 2 k-blocks per CTA.
+  // minimise rounds x (k-blocks per CTA x c + f + exchange) us, the exchange
+  // of a split costing ~1 us for 64-token tiles and 2.5 + 0.3 ks us for
+  // 128-token tiles, with c = 0.28 / f = 5.7 for FP8 and c = 0.52 / f = 6.2
+  // for AWQ (its converters do twice the work per k-block). For AWQ the
+  // paired kernel, ~4.5 + 1.1 us per two-k-block stage when its tiles fit one
+  // wave, is taken when cheaper. All constants are fits of forced plans timed
+  // on B200 over the Qwen2.5-0.5B and Llama-3-8B shapes at M = 128 / 1024. At
+  // least 2 k-blocks per CTA.
   TsPlan best{0, 1};
   if (M <= kDecodeMaxM) return best;
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
@@ -562,6 +565,8 @@ TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N) {
   if (M * N > ((int64_t)1 << 20) && pair_tiles * 4 > sms) return best;
   const int64_t kb = (K + BK - 1) / BK;
   const int64_t wt = (N + BW - 1) / BW;
+  const double c = fmt == 0 ? 0.52 : 0.28;
+  const double f = fmt == 0 ? 6.2 : 5.7;
   double best_cost = 0.0;
   for (int bt : {64, 128}) {
     const int64_t units = wt * ((M + bt - 1) / bt);
@@ -569,13 +574,14 @@ TsPlan prefill_ts_plan(int64_t M, int64_t K, int64_t N) {
       if (ks > 1 && (units * ks > sms || (kb + ks - 1) / ks < 2)) break;
       const int64_t rounds = (units * ks + sms - 1) / sms;
       const double exchange = ks == 1 ? 0.0 : (bt == 64 ? 1.0 : 2.5 + 0.3 * ks);
-      const double cost = (double)rounds * ((double)((kb + ks - 1) / ks) * 0.28 + 5.7 + exchange);
+      const double cost = (double)rounds * ((double)((kb + ks - 1) / ks) * c + f + exchange);
       if (best.tokens_per_tile == 0 || cost < best_cost) {
         best = TsPlan{bt, ks};
         best_cost = cost;
       }
     }
   }
+  if (fmt == 0 && pair_tiles * 2 <= sms && 4.5 + 1.1 * (double)((kb + 1) / 2) < best_cost) return TsPlan{0, 1};
   return best;
 }
 
