@@ -88,8 +88,8 @@ struct TsSmem {
   static constexpr int kX = 0;                              // [NS][KPS] x tiles
   static constexpr int kWc = kX + NS * KPS * kXBytes;       // [NS][KPS] packed weight tiles
   static constexpr int kBar = kWc + NS * KPS * TsFmt<FMT>::kWcBytes;
-  // full_l[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc[2], empty_acc[2], recv
-  static constexpr int kNumBars = 4 * NS + 5;
+  // full_w[NS], full_x[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc[2], empty_acc[2], recv
+  static constexpr int kNumBars = 5 * NS + 5;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kTotal = kAbort + 4;
@@ -132,15 +132,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  // Per stage s: full_l (TMA bytes of x and the packed weight landed), read_w
-  // (the converters read the packed weight), full_a (the converters wrote the
-  // TMEM operand; implies full_l), mma_done (the UMMAs of the stage finished:
-  // frees both the x tiles and the TMEM operand).
-  uint64_t* full_l = bars;
-  uint64_t* read_w = bars + NS;
-  uint64_t* full_a = bars + 2 * NS;
-  uint64_t* mma_done = bars + 3 * NS;
-  uint64_t* full_acc = bars + 4 * NS;
+  // Per stage s: full_w / full_x (TMA bytes of the packed weight / of x
+  // landed), read_w (the converters read the packed weight), full_a (the
+  // converters wrote the TMEM operand and saw full_x), mma_done (the UMMAs of
+  // the stage finished: frees both the x tiles and the TMEM operand).
+  uint64_t* full_w = bars;
+  uint64_t* full_x = bars + NS;
+  uint64_t* read_w = bars + 2 * NS;
+  uint64_t* full_a = bars + 3 * NS;
+  uint64_t* mma_done = bars + 4 * NS;
+  uint64_t* full_acc = bars + 5 * NS;
   uint64_t* empty_acc = full_acc + 2;
   uint64_t* recv = full_acc + 4;  // split K: the other ranks' partial columns landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
@@ -154,7 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&full_l[i], 1);
+      mbar_init(&full_w[i], 1);
+      mbar_init(&full_x[i], 1);
       mbar_init(&read_w[i], kConvWarps);
       mbar_init(&full_a[i], kConvWarps);
       mbar_init(&mma_done[i], 1);
@@ -176,8 +178,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  // everything below may read what the previous kernel on the stream wrote
-  pdl_wait_prior_grids();
+  // The weights (packed tiles, scales, zero points, bias) are static: their
+  // loads and the conversion into TMEM may run before the previous kernel on
+  // the stream finishes. Everything that touches x or y waits for it first
+  // (pdl_wait_prior_grids in the producer before its x loads and in the
+  // epilogue before its stores).
 
   // work units: (tile, K range), token tile fastest; a split tile is one cluster
   const int num_units = p.num_w_tiles * p.num_t_tiles * KS;
@@ -197,6 +202,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
     if (lane == 0) {
       tma_prefetch_desc(&xmap);
       tma_prefetch_desc(&wmap);
+      // packed weight tiles of stage it (k-blocks kb0 .. kb0+nk-1 of unit u)
+      auto load_w = [&](int u, int kb0, int nk, int s) {
+        int wt, tt;
+        unit_tile(u, wt, tt);
+        mbar_arrive_expect_tx(&full_w[s], (uint32_t)nk * TsFmt<FMT>::kWcBytes);
+        for (int i = 0; i < nk; ++i) {
+          const int kb = kb0 + i;
+          tma_load_2d(smem + L::kWc + (s * KPS + i) * TsFmt<FMT>::kWcBytes, &wmap, &full_w[s],
+                      FMT == 0 ? kb * (BK / 8) : kb * BK, wt * BW);
+        }
+      };
+      // the first NS stages' weights before the previous kernel finishes
+      int pre = 0;
+      for (int u = blockIdx.x; u < num_units && pre < NS; u += gridDim.x) {
+        int lo, hi;
+        unit_kb(u, lo, hi);
+        for (int kb0 = lo; kb0 < hi && pre < NS; kb0 += KPS, ++pre) {
+          load_w(u, kb0, hi - kb0 < KPS ? hi - kb0 : KPS, pre);
+        }
+      }
+      pdl_wait_prior_grids();
       int it = 0;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         int wt, tt, lo, hi;
@@ -205,23 +231,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         for (int kb0 = lo; kb0 < hi; kb0 += KPS, ++it) {
           const int s = it % NS;
           const uint32_t ph = ((it / NS) & 1) ^ 1;  // previous use of the stage
-          if (!(ok = mbar_wait(&read_w[s], ph, p.status, 50, abort_flag))) break;
-          if (!(ok = mbar_wait(&mma_done[s], ph, p.status, 57, abort_flag))) break;
           const int nk = hi - kb0 < KPS ? hi - kb0 : KPS;
-          mbar_arrive_expect_tx(&full_l[s], (uint32_t)nk * (L::kXBytes + TsFmt<FMT>::kWcBytes));
+          if (it >= pre) {
+            // a reuse of the stage: the converters are done with its packed
+            // tiles, the UMMAs with its x tiles and TMEM operand
+            if (!(ok = mbar_wait(&read_w[s], ph, p.status, 50, abort_flag))) break;
+            if (!(ok = mbar_wait(&mma_done[s], ph, p.status, 57, abort_flag))) break;
+            load_w(u, kb0, nk, s);
+          }
+          mbar_arrive_expect_tx(&full_x[s], (uint32_t)nk * L::kXBytes);
           for (int i = 0; i < nk; ++i) {
-            const int kb = kb0 + i;
-            tma_load_2d(smem + L::kX + (s * KPS + i) * L::kXBytes, &xmap, &full_l[s], kb * BK, tt * BT);
-            tma_load_2d(smem + L::kWc + (s * KPS + i) * TsFmt<FMT>::kWcBytes, &wmap, &full_l[s],
-                        FMT == 0 ? kb * (BK / 8) : kb * BK, wt * BW);
+            tma_load_2d(smem + L::kX + (s * KPS + i) * L::kXBytes, &xmap, &full_x[s], (kb0 + i) * BK, tt * BT);
           }
         }
       }
       // let in-flight copies land before the CTA can exit
       if (!ok) {
-        const int last = it;
+        const int last = it > pre ? it : pre;
         for (int j = (last > NS ? last - NS : 0); j < last; ++j) {
-          mbar_wait(&full_l[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
+          mbar_wait(&full_w[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
+          if (j < it) mbar_wait(&full_x[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
         }
       }
     }
@@ -315,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       for (int kb0 = lo; kb0 < hi; kb0 += KPS, ++it) {
         const int s = it % NS;
         const uint32_t ph = (it / NS) & 1;
-        if (!(ok = mbar_wait(&full_l[s], ph, p.status, 54, abort_flag))) break;
+        if (!(ok = mbar_wait(&full_w[s], ph, p.status, 54, abort_flag))) break;
         // the TMEM operand stage is free once the UMMAs of its previous use finished
         if (!(ok = mbar_wait(&mma_done[s], ph ^ 1, p.status, 55, abort_flag))) break;
         tc_fence_after();
@@ -344,12 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         if (lane == 0) mbar_arrive(&read_w[s]);
         tmem_st_wait();
         tc_fence_before();
+        // the operand is ready; the UMMAs also need the stage's x tiles
+        if (!(ok = mbar_wait(&full_x[s], ph, p.status, 59, abort_flag))) break;
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_a[s]);
       }
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> y ----------------
+    pdl_wait_prior_grids();  // y may alias memory the previous kernel still used
     const int sub = warp & 3;
     const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
     const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;

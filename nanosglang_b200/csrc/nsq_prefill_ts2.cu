@@ -80,8 +80,8 @@ struct Ts2Smem {
   static constexpr int kY = kWc + NS * KPS * kWcBytes;  // staged y tile: 2 x [256 tokens][64 features]
   static constexpr int kYHalfBytes = kTokRound * 64 * 2;
   static constexpr int kBar = kY + (STAGED ? 2 * kYHalfBytes : 0);
-  // full_l[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc, empty_acc
-  static constexpr int kNumBars = 4 * NS + 2;
+  // full_w[NS], full_x[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc, empty_acc
+  static constexpr int kNumBars = 5 * NS + 2;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kTotal = kAbort + 4;
@@ -119,17 +119,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
-  // Per stage s (both CTAs unless noted): full_l (this CTA's x and packed
-  // weight bytes), read_w (this CTA's converters read the packed weight),
-  // full_a (even CTA: every converter warp of both CTAs wrote its part of the
-  // TMEM operand; each waited for its CTA's full_l first, so full_a implies
-  // both x tiles landed), mma_done (multicast commit: frees the x tile and
-  // the TMEM operand in both CTAs).
-  uint64_t* full_l = bars;
-  uint64_t* read_w = bars + NS;
-  uint64_t* full_a = bars + 2 * NS;
-  uint64_t* mma_done = bars + 3 * NS;
-  uint64_t* full_acc = bars + 4 * NS;
+  // Per stage s (both CTAs unless noted): full_w / full_x (this CTA's packed
+  // weight / x bytes landed), read_w (this CTA's converters read the packed
+  // weight), full_a (even CTA: every converter warp of both CTAs wrote its
+  // part of the TMEM operand and saw its CTA's full_x, so full_a implies both
+  // x tiles landed), mma_done (multicast commit: frees the x tile and the TMEM
+  // operand in both CTAs).
+  uint64_t* full_w = bars;
+  uint64_t* full_x = bars + NS;
+  uint64_t* read_w = bars + 2 * NS;
+  uint64_t* full_a = bars + 3 * NS;
+  uint64_t* mma_done = bars + 4 * NS;
+  uint64_t* full_acc = bars + 5 * NS;
   uint64_t* empty_acc = full_acc + 1;  // even CTA: every epilogue warp of both CTAs
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
@@ -144,7 +145,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&full_l[i], 1);
+      mbar_init(&full_w[i], 1);
+      mbar_init(&full_x[i], 1);
       mbar_init(&read_w[i], kConvWarps);
       mbar_init(&full_a[i], 2 * kConvWarps);
       mbar_init(&mma_done[i], 1);
@@ -162,7 +164,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  pdl_wait_prior_grids();
+  // The weights (packed tiles, scales, zero points, bias) are static: their
+  // loads and the conversion into TMEM may run before the previous kernel on
+  // the stream finishes. The producer waits for it before its x loads, the
+  // epilogue before its stores.
 
   const int num_units = p.num_w_tiles * p.num_t_tiles;  // token tile fastest
   bool ok = true;
@@ -171,6 +176,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
     if (lane == 0) {
       tma_prefetch_desc(&xmap);
       tma_prefetch_desc(&wmap);
+      // packed weight tiles of a stage: k-blocks kb0 .. kb0+nk-1 of weight tile wt
+      auto load_w = [&](int wt, int kb0, int nk, int s) {
+        mbar_arrive_expect_tx(&full_w[s], (uint32_t)nk * L::kWcBytes);
+        for (int i = 0; i < nk; ++i) {
+          const int kb = kb0 + i;
+          tma_load_2d(smem + L::kWc + (s * KPS + i) * L::kWcBytes, &wmap, &full_w[s],
+                      FMT == 0 ? kb * (BK / 8) : kb * BK, wt * (2 * BWC) + (int)rank * BWC);
+        }
+      };
+      // the first NS stages' weights before the previous kernel finishes
+      int pre = 0;
+      for (int u = cid; u < num_units && pre < NS; u += ncl) {
+        for (int st = 0; st < p.num_st && pre < NS; ++st, ++pre) {
+          const int kb0 = st * KPS;
+          load_w(u / p.num_t_tiles, kb0, p.num_kb - kb0 < KPS ? p.num_kb - kb0 : KPS, pre);
+        }
+      }
+      pdl_wait_prior_grids();
       int it = 0;
       for (int u = cid; u < num_units && ok; u += ncl) {
         const int wt = u / p.num_t_tiles;
@@ -180,22 +203,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
         for (int st = 0; st < p.num_st; ++st, ++it) {
           const int s = it % NS;
           const uint32_t ph = ((it / NS) & 1) ^ 1;  // previous use of the stage
-          if (!(ok = mbar_wait(&read_w[s], ph, p.status, 150, abort_flag))) break;
-          if (!(ok = mbar_wait(&mma_done[s], ph, p.status, 151, abort_flag))) break;
           const int kb0 = st * KPS;
           const int nk = p.num_kb - kb0 < KPS ? p.num_kb - kb0 : KPS;
-          mbar_arrive_expect_tx(&full_l[s], (uint32_t)nk * (kXBytes + L::kWcBytes));
+          if (it >= pre) {
+            // a reuse of the stage: the converters are done with its packed
+            // tiles, the UMMAs with its x tiles and TMEM operand
+            if (!(ok = mbar_wait(&read_w[s], ph, p.status, 150, abort_flag))) break;
+            if (!(ok = mbar_wait(&mma_done[s], ph, p.status, 151, abort_flag))) break;
+            load_w(wt, kb0, nk, s);
+          }
+          mbar_arrive_expect_tx(&full_x[s], (uint32_t)nk * kXBytes);
           for (int i = 0; i < nk; ++i) {
-            const int kb = kb0 + i;
-            tma_load_2d(smem + L::kX + (s * KPS + i) * kXBytes, &xmap, &full_l[s], kb * BK, tok0);
-            tma_load_2d(smem + L::kWc + (s * KPS + i) * L::kWcBytes, &wmap, &full_l[s],
-                        FMT == 0 ? kb * (BK / 8) : kb * BK, wt * (2 * BWC) + (int)rank * BWC);
+            tma_load_2d(smem + L::kX + (s * KPS + i) * kXBytes, &xmap, &full_x[s], (kb0 + i) * BK, tok0);
           }
         }
       }
       if (!ok) {  // let in-flight copies land before the CTA can exit
-        for (int j = (it > NS ? it - NS : 0); j < it; ++j) {
-          mbar_wait(&full_l[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
+        const int last = it > pre ? it : pre;
+        for (int j = (last > NS ? last - NS : 0); j < last; ++j) {
+          mbar_wait(&full_w[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
+          if (j < it) mbar_wait(&full_x[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
         }
       }
     }
@@ -269,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
       for (int st = 0; st < p.num_st; ++st, ++it) {
         const int s = it % NS;
         const uint32_t ph = (it / NS) & 1;
-        if (!(ok = mbar_wait(&full_l[s], ph, p.status, 155, abort_flag))) break;
+        if (!(ok = mbar_wait(&full_w[s], ph, p.status, 155, abort_flag))) break;
         // the TMEM operand stage is free once the UMMAs of its previous use finished
         if (!(ok = mbar_wait(&mma_done[s], ph ^ 1, p.status, 156, abort_flag))) break;
         tc_fence_after();
@@ -294,12 +321,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
         if (lane == 0) mbar_arrive(&read_w[s]);
         tmem_st_wait();
         tc_fence_before();
+        // the operand is ready; the UMMAs also need this CTA's x tiles
+        if (!(ok = mbar_wait(&full_x[s], ph, p.status, 158, abort_flag))) break;
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(full_a_leader0 + s * 8);
       }
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> staged tile -> TMA store ----------------
+    pdl_wait_prior_grids();  // y may alias memory the previous kernel still used
     // STAGED: the accumulator is drained into shared memory (bf16/fp16, two
     // 128-byte-swizzled [tokens][64 features] halves; all 256 tokens at once,
     // or 128 per round for FP8) and released as soon as the last round is in
