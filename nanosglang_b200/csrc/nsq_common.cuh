@@ -164,16 +164,6 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
           smem_u32(bar))
       : "memory");
 }
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (fp16 or bf16 in, fp32 acc).
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, A read from tensor memory
 // (M = 128: row i in lane i, K pairs packed two per 32-bit column, 8 columns
 // per K = 16 step).
@@ -282,16 +272,6 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// TMA load into this CTA's shared memory whose completion is counted on the
-// barrier at `bar_cluster_addr` (the even CTA's barrier).
-__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map,
-                                                 uint32_t bar_cluster_addr, int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
-      : "memory");
-}
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(smem_result)),
@@ -304,14 +284,6 @@ __device__ __forceinline__ void tmem_relinquish_pair() {
 __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
-}
-__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                              uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 // Paired UMMA with A read from tensor memory: each CTA's TMEM holds its 128
 // rows of A at the same address; B comes from both CTAs' shared memory (N / 2
@@ -333,43 +305,12 @@ __device__ __forceinline__ void tc_commit_pair_mc(uint64_t* bar, uint16_t cta_ma
       "h"(cta_mask)
       : "memory");
 }
-// Arrive on a barrier of another CTA of the cluster (default semantics). Used
-// after fence.proxy.async by the threads that wrote shared memory the peer's
-// tensor core will read -- the same hand-off CUTLASS's SM100 mixed-input
-// 2-SM mainloop uses. A cluster-scope release here costs about half of the
-// pair kernel's throughput and is not needed for that ordering.
+// Arrive on a barrier of another CTA of the cluster (default semantics). The
+// paired prefill kernel's converters arrive here after tcgen05.wait::st and
+// tcgen05.fence::before_thread_sync on the TMEM operand the pair's UMMA will
+// read; its epilogue warps after their last tcgen05.ld of the accumulator.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait on a barrier that receives arrivals from the peer CTA.
-static __device__ __noinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, DevStatus* st,
-                                                      uint32_t where, volatile int* abort_flag) {
-  const unsigned long long t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-        if (st != nullptr && atomicCAS(&st->code, 0u, (unsigned)NSQ_EDEVICE_TIMEOUT) == 0u) {
-          st->where = where;
-          st->block = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-        }
-        if (abort_flag != nullptr) *abort_flag = 1;
-        __threadfence();
-        return false;
-      }
-    }
-  }
 }
 
 // TMA store of a shared-memory tile (bulk-group completion).
@@ -470,11 +411,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
