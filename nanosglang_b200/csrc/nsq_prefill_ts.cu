@@ -398,12 +398,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       const float bn = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
       const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16) + TM::kAcc + acc * BT;
       const int m0 = tt * BT;
+      // two 32-token chunks per TMEM wait (tcgen05.wait::ld waits for every
+      // load in flight, so batching the loads, not prefetching, hides them)
+      const int nc = (p.M - m0 + 31) / 32 < BT / 32 ? (p.M - m0 + 31) / 32 : BT / 32;
 #pragma unroll 1
-      for (int c = 0; c < BT / 32 && m0 + c * 32 < p.M; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
+      for (int c = 0; c < nc; c += 2) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, ra);
+        if (c + 1 < nc) tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
         tmem_ld_wait();
-        ts_store_tokens<BF16, 32>(y, p.M, p.N, n, m0 + c * 32, r, wscale, has_bias, bn, lane);
+        ts_store_tokens<BF16, 32>(y, p.M, p.N, n, m0 + c * 32, ra, wscale, has_bias, bn, lane);
+        if (c + 1 < nc) ts_store_tokens<BF16, 32>(y, p.M, p.N, n, m0 + (c + 1) * 32, rb, wscale, has_bias, bn, lane);
       }
       tc_fence_before();
       __syncwarp();
@@ -412,6 +417,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   }
 
   if (KS > 1) {
+    // the first four 16-column chunks of the accumulator go to registers
+    // before the cluster barrier (one TMEM wait, overlapping the barrier)
+    constexpr int kBatch = 4;
+    uint32_t rb[kBatch][16];
+    const uint32_t taddr0 = tmem_base + ((uint32_t)((warp & 3) * 32) << 16);  // accumulator 0
+    if (warp >= kWarpEpi0 && ok) {
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) tmem_ld_32x32b_x16(taddr0 + i * kXChunk, rb[i]);
+      tmem_ld_wait();
+    }
     // every CTA of the cluster is done with its main loop: all x rings are
     // free to receive the partial columns
     __syncwarp();
@@ -426,14 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       const uint32_t units = (uint32_t)cpo * 4;  // 16-byte units per slot row
       const uint32_t slot_bytes = (uint32_t)BW * units * 16;
       const uint32_t row_off = (uint32_t)r_in * units * 16;
-      const uint32_t taddr = tmem_base + ((uint32_t)(sub * 32) << 16);  // accumulator 0
       const uint32_t rbar = smem_u32(recv);
       // slot q (the partial of rank q) of an owner: [128 rows][cpo chunks of 16 fp32]
-#pragma unroll 1
-      for (int c = 0; c < BT / kXChunk; ++c) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(taddr + c * kXChunk, r);
-        tmem_ld_wait();
+      auto send = [&](const uint32_t (&r)[16], int c) {
         const int owner = c / cpo, lc = c - owner * cpo;
         const uint32_t local = smem_u32(smem + L::kX) + me * slot_bytes + row_off;
 #pragma unroll
@@ -447,6 +457,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
                            __uint_as_float(r[4 * j + 3]), dsmem_map(rbar, (uint32_t)owner));
           }
         }
+      };
+#pragma unroll
+      for (int c0 = 0; c0 < BT / kXChunk; c0 += kBatch) {
+        if (c0 > 0) {  // later batches (128-token tiles): load, then one wait
+#pragma unroll
+          for (int i = 0; i < kBatch; ++i) tmem_ld_32x32b_x16(taddr0 + (c0 + i) * kXChunk, rb[i]);
+          tmem_ld_wait();
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) send(rb[i], c0 + i);
       }
       named_bar_sync(3, kEpiWarps * 32);  // this CTA's own slot is written
       if (mbar_wait(recv, 0, p.status, 58, nullptr)) {
