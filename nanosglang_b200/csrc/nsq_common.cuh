@@ -157,24 +157,78 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// Arrive on `bar` once every tcgen05 op issued so far by this thread completes.
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+// Arrive on `bar` once every tcgen05 op issued so far by the elected lane of
+// this (converged) warp completes. The issuing warps run their loops
+// converged; one lane (elect.sync) issues, the others keep the warp together.
+__device__ __forceinline__ void tc_commit_elect(uint64_t* bar) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
           smem_u32(bar))
       : "memory");
 }
-// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, A read from tensor memory
-// (M = 128: row i in lane i, K pairs packed two per 32-bit column, 8 columns
-// per K = 16 step).
-__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, over one or two 64-column
+// k-blocks (4 UMMAs of K = 16 each), issued back to back by the elected lane
+// of a converged warp. A is read from tensor memory (M = 128 rows per CTA: row
+// i in lane i, K pairs packed two per 32-bit column; k-block j at a + 32 j, +8
+// columns per K = 16 step); B from the 128-byte-swizzled x tile of k-block j
+// (descriptor b_j, +32 bytes per step). Only the first UMMA takes
+// `accumulate`; the others accumulate. CG = 2: the paired form (each CTA's
+// TMEM holds its 128 rows of A at the same address; B comes from both CTAs'
+// shared memory, N / 2 rows each at the same offset; D lands in each CTA's
+// TMEM, its 128 rows x N).
+// Why one asm block with every operand in its own register: issued one per
+// statement (a predicate set-up and the descriptor arithmetic between them,
+// from a lone lane), a UMMA costs the issuing thread 100-130 cycles on B200,
+// 3.5x the tensor time of a 128 x 64 x 16 step; issued this way a chain of
+// them runs at 34 / 67 / 131 cycles for N = 64 / 128 / 256 (measured), the
+// tensor pipe's own pace.
+#define NSQ_UMMA_TS_PRE \
+  "{\n\t.reg .pred e, p, t;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"
+template <int CG, int KB>
+__device__ __forceinline__ void umma_ts_kblocks_elect(uint32_t d, uint32_t a, uint64_t b0, uint64_t b1,
+                                                      uint32_t idesc, uint32_t accumulate) {
+  static_assert((CG == 1 || CG == 2) && (KB == 1 || KB == 2), "cta_group 1/2, one or two k-blocks");
+#define NSQ_MMA1 "@e tcgen05.mma.cta_group::1.kind::f16 [%0], "
+#define NSQ_MMA2 "@e tcgen05.mma.cta_group::2.kind::f16 [%0], "
+  if constexpr (KB == 2) {
+#define NSQ_X8(M)                                                                                   \
+  NSQ_UMMA_TS_PRE "setp.ne.b32 p, %18, 0;\n\tsetp.eq.b32 t, %18, %18;\n\t"                          \
+  M "[%1], %9, %17, p;\n\t" M "[%2], %10, %17, t;\n\t" M "[%3], %11, %17, t;\n\t"                  \
+  M "[%4], %12, %17, t;\n\t" M "[%5], %13, %17, t;\n\t" M "[%6], %14, %17, t;\n\t"                 \
+  M "[%7], %15, %17, t;\n\t" M "[%8], %16, %17, t;\n\t}"
+#define NSQ_X8_ARGS                                                                                 \
+  "r"(d), "r"(a), "r"(a + 8), "r"(a + 16), "r"(a + 24), "r"(a + 32), "r"(a + 40), "r"(a + 48),      \
+      "r"(a + 56), "l"(b0), "l"(b0 + 2), "l"(b0 + 4), "l"(b0 + 6), "l"(b1), "l"(b1 + 2), "l"(b1 + 4), \
+      "l"(b1 + 6), "r"(idesc), "r"(accumulate)
+    if constexpr (CG == 1) {
+      asm volatile(NSQ_X8(NSQ_MMA1)::NSQ_X8_ARGS : "memory");
+    } else {
+      asm volatile(NSQ_X8(NSQ_MMA2)::NSQ_X8_ARGS : "memory");
+    }
+#undef NSQ_X8
+#undef NSQ_X8_ARGS
+  } else {
+    (void)b1;
+#define NSQ_X4(M)                                                                          \
+  NSQ_UMMA_TS_PRE "setp.ne.b32 p, %10, 0;\n\tsetp.eq.b32 t, %10, %10;\n\t"                 \
+  M "[%1], %5, %9, p;\n\t" M "[%2], %6, %9, t;\n\t" M "[%3], %7, %9, t;\n\t" M "[%4], %8, %9, t;\n\t}"
+#define NSQ_X4_ARGS                                                                              \
+  "r"(d), "r"(a), "r"(a + 8), "r"(a + 16), "r"(a + 24), "l"(b0), "l"(b0 + 2), "l"(b0 + 4), "l"(b0 + 6), \
+      "r"(idesc), "r"(accumulate)
+    if constexpr (CG == 1) {
+      asm volatile(NSQ_X4(NSQ_MMA1)::NSQ_X4_ARGS : "memory");
+    } else {
+      asm volatile(NSQ_X4(NSQ_MMA2)::NSQ_X4_ARGS : "memory");
+    }
+#undef NSQ_X4
+#undef NSQ_X4_ARGS
+  }
+#undef NSQ_MMA1
+#undef NSQ_MMA2
 }
+#undef NSQ_UMMA_TS_PRE
 
 // 16 registers per thread -> 32 lanes x 16 consecutive 32-bit TMEM columns.
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -285,23 +339,13 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
-// Paired UMMA with A read from tensor memory: each CTA's TMEM holds its 128
-// rows of A at the same address; B comes from both CTAs' shared memory (N / 2
-// rows each, same offset), D lands in each CTA's TMEM (its 128 rows x N).
-__device__ __forceinline__ void umma_f16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
-                                                 uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // Arrive on the barrier at the same offset in every CTA of `cta_mask` once all
-// tcgen05 ops issued so far by this thread complete.
-__device__ __forceinline__ void tc_commit_pair_mc(uint64_t* bar, uint16_t cta_mask) {
+// tcgen05 ops issued so far by the elected lane of this (converged) warp complete.
+__device__ __forceinline__ void tc_commit_pair_mc_elect(uint64_t* bar, uint16_t cta_mask) {
   asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
       "h"(cta_mask)
       : "memory");
 }

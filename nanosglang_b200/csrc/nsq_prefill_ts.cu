@@ -20,9 +20,10 @@
 //   warp 0        TMA producer: per stage KPS x tiles [BT tokens x 64]
 //                 (128-byte swizzle) and KPS packed weight tiles [128 rows x
 //                 64 columns] of the reference layout, NS-stage ring.
-//   warp 1        TMEM allocation; lane 0 issues 128 x BT x 16 UMMAs with A
-//                 from TMEM; one barrier wait and one commit per stage (8
-//                 UMMAs): each barrier operation in the issuer opens a bubble
+//   warp 1        TMEM allocation; runs the issue loop converged, and one
+//                 elected lane issues each stage's 8 UMMAs (128 x BT x 16, A
+//                 from TMEM) as one block; one barrier wait and one commit per
+//                 stage: each barrier operation in the issuer opens a bubble
 //                 of a few hundred cycles in the tensor pipe on B200.
 //   warps 2..9    converters: warp w serves TMEM sub-partition w % 4 (32 weight
 //                 rows, one per lane) and half (w - 2) / 4 of each k-block;
@@ -50,7 +51,7 @@ namespace {
 
 constexpr int BW = 128;  // weight rows per tile (UMMA M, TMEM lanes)
 constexpr int BK = 64;   // columns per k-block
-constexpr int KPS = 2;   // k-blocks per stage
+constexpr int KPS = 2;   // k-blocks per stage (the UMMA issue block covers two)
 constexpr int NS = 4;    // stages
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
@@ -255,43 +256,43 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       }
     }
   } else if (warp == kWarpMma) {
-    if (lane == 0) {
-      int it = 0, tcount = 0;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++tcount) {
-        int wt, tt, lo, hi;
-        unit_tile(u, wt, tt);
-        unit_kb(u, lo, hi);
-        // UMMA N: the tile's tokens rounded up to 16 (the x rows past M are
-        // zero-filled by TMA; their accumulator columns are never stored)
-        int n_eff = p.M - tt * BT;
-        n_eff = n_eff > BT ? BT : ((n_eff + 15) & ~15);
-        const uint32_t idesc = umma_idesc_f16(BF16, BW, n_eff);
-        const int acc = tcount & 1;
-        if (!(ok = mbar_wait(&empty_acc[acc], ((tcount >> 1) & 1) ^ 1, p.status, 51, abort_flag))) break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + TM::kAcc + acc * BT;
-        for (int kb0 = lo; kb0 < hi; kb0 += KPS, ++it) {
-          const int s = it % NS;
-          if (!(ok = mbar_wait(&full_a[s], (it / NS) & 1, p.status, 53, abort_flag))) break;
-          tc_fence_after();
-          const int nk = hi - kb0 < KPS ? hi - kb0 : KPS;
-#pragma unroll
-          for (int i = 0; i < KPS; ++i) {
-            if (i < nk) {
-              const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kX + (s * KPS + i) * L::kXBytes));
-              const uint32_t a = tmem_base + TM::kA + (s * KPS + i) * 32;
-#pragma unroll
-              for (int kk = 0; kk < BK / 16; ++kk) {
-                // A: +8 TMEM columns per 16 K; B: +32 bytes inside the swizzled row
-                umma_f16_ts(d, a + 8 * kk, bdesc + 2 * kk, idesc, (kb0 > lo || i > 0 || kk > 0) ? 1u : 0u);
-              }
-            }
-          }
-          tc_commit(&mma_done[s]);
-        }
+    // The whole warp runs the loop (every lane waits on the barriers, so the
+    // warp stays converged); one elected lane issues the UMMAs of a stage as
+    // one block and the commits.
+    int it = 0, tcount = 0;
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++tcount) {
+      int wt, tt, lo, hi;
+      unit_tile(u, wt, tt);
+      unit_kb(u, lo, hi);
+      // UMMA N: the tile's tokens rounded up to 16 (the x rows past M are
+      // zero-filled by TMA; their accumulator columns are never stored)
+      int n_eff = p.M - tt * BT;
+      n_eff = n_eff > BT ? BT : ((n_eff + 15) & ~15);
+      const uint32_t idesc = umma_idesc_f16(BF16, BW, n_eff);
+      const int acc = tcount & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&empty_acc[acc], ((tcount >> 1) & 1) ^ 1, p.status, 51, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + TM::kAcc + acc * BT;
+      for (int kb0 = lo; kb0 < hi; kb0 += KPS, ++it) {
+        const int s = it % NS;
+        ok = __all_sync(0xffffffffu, mbar_wait(&full_a[s], (it / NS) & 1, p.status, 53, abort_flag));
         if (!ok) break;
-        tc_commit(&full_acc[acc]);
+        tc_fence_after();
+        // A: the stage's TMEM operand (32 columns per k-block); B: its x tiles
+        const uint32_t a = tmem_base + TM::kA + s * KPS * 32;
+        const uint64_t b0 = sw128_kmajor_desc(smem_u32(smem + L::kX + s * KPS * L::kXBytes));
+        const uint32_t acc_in = kb0 > lo ? 1u : 0u;
+        if (hi - kb0 >= 2) {
+          const uint64_t b1 = sw128_kmajor_desc(smem_u32(smem + L::kX + (s * KPS + 1) * L::kXBytes));
+          umma_ts_kblocks_elect<1, 2>(d, a, b0, b1, idesc, acc_in);
+        } else {
+          umma_ts_kblocks_elect<1, 1>(d, a, b0, 0, idesc, acc_in);
+        }
+        tc_commit_elect(&mma_done[s]);
       }
+      if (!ok) break;
+      tc_commit_elect(&full_acc[acc]);
     }
   } else if (warp < kWarpEpi0) {
     // ---------------- converters: packed weight -> TMEM operand ----------------

@@ -19,8 +19,9 @@
 //                 and this CTA's packed weight tile [128 rows x 64 columns],
 //                 KPS of each per stage, NS-stage ring, completion on this
 //                 CTA's own barrier.
-//   warp 1        TMEM allocation (512 columns, paired); in the even CTA, lane
-//                 0 issues the UMMAs and the multicast commits.
+//   warp 1        TMEM allocation (512 columns, paired); in the even CTA it
+//                 runs the issue loop converged, and one elected lane issues
+//                 each stage's 8 UMMAs as one block and the multicast commits.
 //   warps 2..9    converters: warp w serves TMEM sub-partition w % 4 (32
 //                 weight rows, one per lane) and half (w - 2) / 4 of the 64
 //                 columns; tcgen05.st into an NS-stage TMEM operand ring, then
@@ -49,7 +50,7 @@ namespace {
 constexpr int BWC = 128;  // weight rows per CTA (TMEM lanes); the pair tile is 256
 constexpr int BTP = 256;  // tokens per pair tile (UMMA N); 128 per CTA
 constexpr int BK = 64;
-constexpr int KPS = 2;    // k-blocks per stage: one barrier round per 8 UMMAs
+constexpr int KPS = 2;    // k-blocks per stage: one barrier round per 8 UMMAs (one issue block)
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpConv0 = 2;
@@ -227,34 +228,36 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
       }
     }
   } else if (warp == kWarpMma) {
-    if (leader && lane == 0) {
+    // Even CTA: the whole warp runs the loop (every lane waits on the
+    // barriers, so the warp stays converged); one elected lane issues the
+    // UMMAs of a stage as one block and the multicast commits.
+    if (leader) {
       int it = 0, tcount = 0;
       for (int u = cid; u < num_units && ok; u += ncl, ++tcount) {
         const int tt = u % p.num_t_tiles;
         const uint32_t idesc = umma_idesc_f16(BF16, 2 * BWC, ts2_n_eff(p.M, tt));
-        if (!(ok = mbar_wait(empty_acc, (tcount & 1) ^ 1, p.status, 152, abort_flag))) break;
+        ok = __all_sync(0xffffffffu, mbar_wait(empty_acc, (tcount & 1) ^ 1, p.status, 152, abort_flag));
+        if (!ok) break;
         tc_fence_after();
         for (int st = 0; st < p.num_st; ++st, ++it) {
           const int s = it % NS;
-          if (!(ok = mbar_wait(&full_a[s], (it / NS) & 1, p.status, 153, abort_flag))) break;
+          ok = __all_sync(0xffffffffu, mbar_wait(&full_a[s], (it / NS) & 1, p.status, 153, abort_flag));
+          if (!ok) break;
           tc_fence_after();
-          const int nk = p.num_kb - st * KPS < KPS ? p.num_kb - st * KPS : KPS;
-#pragma unroll
-          for (int i = 0; i < KPS; ++i) {
-            if (i < nk) {
-              const uint64_t bdesc = sw128_kmajor_desc(smem_u32(smem + L::kX + (s * KPS + i) * kXBytes));
-              const uint32_t a = tmem_base + kTmemA + (s * KPS + i) * 32;
-#pragma unroll
-              for (int kk = 0; kk < BK / 16; ++kk) {
-                // A: +8 TMEM columns per 16 K; B: +32 bytes inside the swizzled row
-                umma_f16_pair_ts(tmem_base, a + 8 * kk, bdesc + 2 * kk, idesc, (st > 0 || i > 0 || kk > 0) ? 1u : 0u);
-              }
-            }
+          // A: the stage's TMEM operand (32 columns per k-block); B: its x tiles
+          const uint32_t a = tmem_base + kTmemA + s * KPS * 32;
+          const uint64_t b0 = sw128_kmajor_desc(smem_u32(smem + L::kX + s * KPS * kXBytes));
+          const uint32_t acc_in = st > 0 ? 1u : 0u;
+          if (p.num_kb - st * KPS >= 2) {
+            const uint64_t b1 = sw128_kmajor_desc(smem_u32(smem + L::kX + (s * KPS + 1) * kXBytes));
+            umma_ts_kblocks_elect<2, 2>(tmem_base, a, b0, b1, idesc, acc_in);
+          } else {
+            umma_ts_kblocks_elect<2, 1>(tmem_base, a, b0, 0, idesc, acc_in);
           }
-          tc_commit_pair_mc(&mma_done[s], 0x3);
+          tc_commit_pair_mc_elect(&mma_done[s], 0x3);
         }
         if (!ok) break;
-        tc_commit_pair_mc(full_acc, 0x3);
+        tc_commit_pair_mc_elect(full_acc, 0x3);
       }
     }
   } else if (warp < kWarpEpi0) {
