@@ -427,13 +427,15 @@ __device__ __forceinline__ void cluster_arrive_rel() {
 __device__ __forceinline__ void cluster_wait_acq() {
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
 }
-// 16-byte store into another CTA's shared memory, counted on its barrier.
-__device__ __forceinline__ void st_async_f32x4(uint32_t cluster_addr, float a, float b, float c, float d,
-                                               uint32_t cluster_bar) {
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this CTA's shared memory into another CTA's, counted on the barrier
+// `bar_cluster` in the destination CTA.
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                    uint32_t bar_cluster) {
   asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-          cluster_addr),
-      "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
       : "memory");
 }
 __device__ __forceinline__ uint32_t dsmem_map(uint32_t smem_addr, uint32_t cta_rank) {

@@ -34,10 +34,12 @@
 //                 rounding, stores of feature pairs exchanged between lanes.
 // Without a K split the accumulators are double-buffered (the epilogue of tile
 // i overlaps the main loop of tile i + 1). With a K split of ks CTAs per tile
-// (a cluster), every CTA owns BT / ks token columns of the tile: after the
-// main loops it sends its other fp32 columns into the owners' idle x rings
-// (st.async counted on the owner's transaction barrier) and sums the partials
-// of its own columns in rank order, so the result does not depend on timing.
+// (a cluster), every CTA owns BT / ks token columns of the tile: after its
+// main loop it stages its other fp32 columns in its own idle x ring and sends
+// them with one bulk shared-to-shared copy per owner into the owner's idle x
+// ring (counted on the owner's transaction barrier, once the owner signalled
+// that its UMMAs are done), and sums the partials of its own columns in rank
+// order, so the result does not depend on timing.
 // Every wait is bounded.
 #include <atomic>
 
@@ -89,8 +91,9 @@ struct TsSmem {
   static constexpr int kX = 0;                              // [NS][KPS] x tiles
   static constexpr int kWc = kX + NS * KPS * kXBytes;       // [NS][KPS] packed weight tiles
   static constexpr int kBar = kWc + NS * KPS * TsFmt<FMT>::kWcBytes;
-  // full_w[NS], full_x[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc[2], empty_acc[2], recv
-  static constexpr int kNumBars = 5 * NS + 5;
+  // full_w[NS], full_x[NS], read_w[NS], full_a[NS], mma_done[NS], full_acc[2], empty_acc[2],
+  // recv, peers_free, peers_received
+  static constexpr int kNumBars = 5 * NS + 7;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kTotal = kAbort + 4;
@@ -98,8 +101,9 @@ struct TsSmem {
   static constexpr int kAlloc = kNeed > kMinSmem ? kNeed : kMinSmem;
   static_assert(kXBytes % 1024 == 0, "x stages stay 1 KB aligned");
   static_assert(kAlloc <= 227 * 1024, "shared memory per CTA");
-  // split K: the partial tiles of all ranks (BW x BT fp32) fit in the x ring
-  static_assert(kWc - kX >= BW * BT * 4, "split-K receive slots");
+  // split K: the receive slots of all ranks and the staged partials of the
+  // other owners (together less than 2 x BW x BT fp32) fit in the x ring
+  static_assert(kWc - kX >= 2 * BW * BT * 4, "split-K receive and staging slots");
 };
 
 struct TsParams {
@@ -144,7 +148,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   uint64_t* mma_done = bars + 4 * NS;
   uint64_t* full_acc = bars + 5 * NS;
   uint64_t* empty_acc = full_acc + 2;
-  uint64_t* recv = full_acc + 4;  // split K: the other ranks' partial columns landed
+  // split K: the other ranks' partial columns landed here (recv); every
+  // other rank's receive slots are free (peers_free); every other rank
+  // received this CTA's partials, so their source tiles were read (peers_received)
+  uint64_t* recv = full_acc + 4;
+  uint64_t* peers_free = full_acc + 5;
+  uint64_t* peers_received = full_acc + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbort);
 
@@ -167,6 +176,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       mbar_init(&empty_acc[i], kEpiWarps);
     }
     mbar_init(recv, 1);
+    if (KS > 1) {
+      mbar_init(peers_free, KS - 1);
+      mbar_init(peers_received, KS - 1);
+    }
     fence_barrier_init();
     if (KS > 1) mbar_arrive_expect_tx(recv, (uint32_t)((KS - 1) * BW * cpo * kXChunk * 4));
   }
@@ -178,6 +191,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // split K: this CTA's barriers are initialised; every thread waits for the
+  // other ranks' arrivals before its first remote operation (or at its end)
+  if (KS > 1) cluster_arrive_rel();
 
   // The weights (packed tiles, scales, zero points, bias) are static: their
   // loads and the conversion into TMEM may run before the previous kernel on
@@ -418,23 +434,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
   }
 
   if (KS > 1) {
-    // the first four 16-column chunks of the accumulator go to registers
-    // before the cluster barrier (one TMEM wait, overlapping the barrier)
+    // The exchange. Each rank owns cpo 16-column chunks of the tile: its own
+    // partial of them goes straight into its receive slot `me`; its partials
+    // of every other owner's chunks are staged locally in that owner's slot
+    // layout and sent with one bulk shared-to-shared copy per owner, counted
+    // on the owner's recv barrier, once the owner said that its receive
+    // slots (its x ring) are free. Receivers sum the KS slots in rank order
+    // (the result does not depend on timing) and then tell every sender that
+    // its staged tiles were read.
+    // The first four 16-column chunks of the accumulator go to registers first
+    // (one TMEM wait).
     constexpr int kBatch = 4;
     uint32_t rb[kBatch][16];
     const uint32_t taddr0 = tmem_base + ((uint32_t)((warp & 3) * 32) << 16);  // accumulator 0
-    if (warp >= kWarpEpi0 && ok) {
+    if (warp >= kWarpEpi0) {
+      if (ok) {
 #pragma unroll
-      for (int i = 0; i < kBatch; ++i) tmem_ld_32x32b_x16(taddr0 + i * kXChunk, rb[i]);
-      tmem_ld_wait();
+        for (int i = 0; i < kBatch; ++i) tmem_ld_32x32b_x16(taddr0 + i * kXChunk, rb[i]);
+        tmem_ld_wait();
+      }
+      cluster_wait_acq();  // every rank's barriers are initialised
     }
-    // every CTA of the cluster is done with its main loop: all x rings are
-    // free to receive the partial columns
-    __syncwarp();
-    cluster_arrive_rel();
-    cluster_wait_acq();
     if (warp >= kWarpEpi0 && ok) {
-      const int me = (int)cluster_ctarank();
+      const uint32_t me = cluster_ctarank();
+      const int etid = threadIdx.x - kWarpEpi0 * 32;
       const int sub = warp & 3;
       const int r_in = sub * 32 + lane;  // this thread's row (output feature) of the tile
       int wt, tt;
@@ -442,21 +465,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
       const uint32_t units = (uint32_t)cpo * 4;  // 16-byte units per slot row
       const uint32_t slot_bytes = (uint32_t)BW * units * 16;
       const uint32_t row_off = (uint32_t)r_in * units * 16;
-      const uint32_t rbar = smem_u32(recv);
-      // slot q (the partial of rank q) of an owner: [128 rows][cpo chunks of 16 fp32]
-      auto send = [&](const uint32_t (&r)[16], int c) {
-        const int owner = c / cpo, lc = c - owner * cpo;
-        const uint32_t local = smem_u32(smem + L::kX) + me * slot_bytes + row_off;
+      // receive slots q = 0..KS-1 at the start of the (idle) x ring, then the
+      // staged partials of the other owners (o < me at o, o > me at o - 1)
+      const uint32_t xbase = smem_u32(smem + L::kX);
+      const uint32_t stage0 = xbase + (uint32_t)KS * slot_bytes;
+      auto stage_of = [&](uint32_t o) { return stage0 + (o < me ? o : o - 1) * slot_bytes; };
+      // this CTA's UMMAs are done: its receive slots are free for the others
+      if (etid == 0) {
+        for (uint32_t q = 0; q < (uint32_t)KS; ++q) {
+          if (q != me) mbar_arrive_cluster(dsmem_map(smem_u32(peers_free), q));
+        }
+      }
+      auto put = [&](const uint32_t (&r)[16], int c) {
+        const uint32_t owner = (uint32_t)(c / cpo);
+        const int lc = c - (int)owner * cpo;
+        const uint32_t dst = (owner == me ? xbase + me * slot_bytes : stage_of(owner)) + row_off;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint32_t off = ts_slot_unit((uint32_t)(lc * 4 + j), (uint32_t)r_in, units);
-          if (owner == me) {
-            sts128(local + off, r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-          } else {
-            st_async_f32x4(dsmem_map(local + off, (uint32_t)owner), __uint_as_float(r[4 * j]),
-                           __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
-                           __uint_as_float(r[4 * j + 3]), dsmem_map(rbar, (uint32_t)owner));
-          }
+          sts128(dst + ts_slot_unit((uint32_t)(lc * 4 + j), (uint32_t)r_in, units), r[4 * j], r[4 * j + 1],
+                 r[4 * j + 2], r[4 * j + 3]);
         }
       };
 #pragma unroll
@@ -467,15 +494,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
           tmem_ld_wait();
         }
 #pragma unroll
-        for (int i = 0; i < kBatch; ++i) send(rb[i], c0 + i);
+        for (int i = 0; i < kBatch; ++i) put(rb[i], c0 + i);
       }
-      named_bar_sync(3, kEpiWarps * 32);  // this CTA's own slot is written
+      fence_proxy_async_smem();           // the staged tiles are read by bulk copies
+      named_bar_sync(3, kEpiWarps * 32);  // every partial is in place
+      if (etid == 0 && mbar_wait(peers_free, 0, p.status, 60, nullptr)) {
+        const uint32_t rbar = smem_u32(recv);
+        for (uint32_t q = 0; q < (uint32_t)KS; ++q) {
+          if (q != me) {
+            bulk_copy_s2cluster(dsmem_map(xbase + me * slot_bytes, q), stage_of(q), slot_bytes, dsmem_map(rbar, q));
+          }
+        }
+      }
       if (mbar_wait(recv, 0, p.status, 58, nullptr)) {
+        if (etid == 0) {  // the senders' staged tiles are read
+          for (uint32_t q = 0; q < (uint32_t)KS; ++q) {
+            if (q != me) mbar_arrive_cluster(dsmem_map(smem_u32(peers_received), q));
+          }
+        }
         const int n = wt * BW + r_in;
         const float wscale = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
         const bool has_bias = p.bias_dtype != NSQ_DTYPE_NONE;
         const float bn = (has_bias && n < p.N) ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
-        const uint32_t base = smem_u32(smem + L::kX) + row_off;
+        const uint32_t base = xbase + row_off;
 #pragma unroll 1
         for (int lc = 0; lc < cpo; ++lc) {
           float v[16];
@@ -495,12 +536,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
           uint32_t rr[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) rr[i] = __float_as_uint(v[i]);
-          ts_store_tokens<BF16, 16>(static_cast<uint16_t*>(p.y), p.M, p.N, n, tt * BT + (me * cpo + lc) * kXChunk,
+          ts_store_tokens<BF16, 16>(static_cast<uint16_t*>(p.y), p.M, p.N, n, tt * BT + ((int)me * cpo + lc) * kXChunk,
                                     rr, wscale, has_bias, bn, lane);
         }
+        // the CTA leaves only after the other ranks read its staged tiles
+        if (etid == 0) mbar_wait(peers_received, 0, p.status, 61, nullptr);
       }
       tc_fence_before();  // the TMEM reads above precede the deallocation
     }
+    if (warp < kWarpEpi0) cluster_wait_acq();
   }
 
   pdl_launch_dependents();
