@@ -543,6 +543,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         if (etid == 0) mbar_wait(peers_received, 0, p.status, 61, nullptr);
       }
       tc_fence_before();  // the TMEM reads above precede the deallocation
+    } else if (warp == kWarpEpi0 && lane == 0) {
+      // This rank gave up (a bounded wait ran out). The other ranks may still
+      // arrive on its barriers and copy into its shared memory: let those
+      // land (bounded) before the CTA can exit.
+      mbar_wait(peers_free, 0, nullptr, 0, nullptr);
+      mbar_wait(recv, 0, nullptr, 0, nullptr);
     }
     if (warp < kWarpEpi0) cluster_wait_acq();
   }
