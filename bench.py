@@ -19,17 +19,21 @@ absmax/448 scale, bf16 N(0,1) activations. Random init, synthetic data.
   awq_config0  BASELINE config 0: AWQ W4A16 M=16, K=896, N=9728, cold-L2
            per-linear mean inside a CUDA graph over > 2x L2 of distinct
            weight copies; GB/s vs the measured HBM copy bandwidth.
+  parity   every one of the 42 outputs of the timed graph against an fp32
+           product of the bit-exact dequantised weight (max relative
+           Frobenius error; the bar is 1e-2). Under torchrun the sharded
+           outputs are gathered and checked against the unsharded layer.
   cpu_baseline  the CPU oracle (numpy restatement of the reference path) on
-           the box's host cores, on a bounded sample (M capped at 1024 rows).
+           all of the box's host cores, on the same 42 linears.
 
 --gpus N (under torchrun): tensor parallel over the same sweep, q/k/v/gate/up
-column-parallel, o/down row-parallel + NCCL all_reduce; max-over-ranks time.
+column-parallel, o/down row-parallel + NCCL all_reduce; max-over-ranks time;
+`tp_breakdown` times the linears alone and the 12 all-reduces alone.
 --impl reference: the CPU oracle alone on the same workload (rank 0 only).
---ncu-case NAME: run a few launches of one kernel class and exit (no timing,
-no JSON), for Nsight Compute captures of a small case:
+--ncu-case NAME: run a few launches of one kernel and exit (no timing, no
+JSON), for Nsight Compute captures of a small case (one kernel, <= 4 launches):
   prefill        FP8 gate shape, M=16384 (paired-CTA TMEM-operand GEMM), 3 launches
-  sweep_prefill  the sweep's M > 64 linears once each (the roofline kernel's launches)
-  decode         the sweep's M <= 64 linears once each
+  down8192       FP8 down 4864->896 at M=8192 (the sweep's paired-kernel launch), 3 launches
   awq0           config-0 AWQ linear (M=16, K=896, N=9728), 4 launches
 """
 
@@ -54,10 +58,17 @@ SHAPES = [("q", 896, 896), ("k", 896, 128), ("v", 896, 128), ("o", 896, 896),
           ("gate", 896, 4864), ("up", 896, 4864), ("down", 4864, 896)]  # (name, K, N)
 MS = [1, 8, 32, 128, 1024, 8192]
 ROW_PARALLEL = {"o", "down"}
-CPU_SAMPLE_MAX_M = 1024
+PARITY_TOL = 1e-2
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "FP8 W8A16 linear throughput, Qwen2.5-0.5B projection sweep (config 1)"
 WORKLOAD = "config1_fp8_sweep_qwen2.5-0.5b_7shapes_x_M{1,8,32,128,1024,8192}"
+
+
+def sweep_config(world):
+    """The workload description both arms print (identical by construction)."""
+    return {"workload": WORKLOAD, "linears_per_step": len(SHAPES) * len(MS),
+            "weights": "fp8 e4m3, per-tensor scale", "activations": "bf16 N(0,1)", "parallelism": f"tp{world}",
+            "l2": "flushed between timed steps (256 MiB write)"}
 
 
 def load_peaks():
@@ -69,21 +80,23 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "traffic_config1_sweep_launches.txt")
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "traffic_prefill_ts2_kernel_fp8_down_m8192.txt")
 
 
-def profiled_traffic(case):
-    """Mean DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum) of the
-    sweep's prefill or decode launches, from the committed capture summary; None if absent."""
+def profiled_traffic():
+    """DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one launch
+    of the sweep's top prefill launch (FP8 down at M = 8192) and its algorithmic
+    bytes, from the committed one-kernel capture summary; None if absent."""
+    out = {}
     try:
         with open(TRAFFIC_PROFILE) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == case:
-                    return int(float(parts[2]))
+                if len(parts) == 2 and parts[0] in ("traffic_bytes_per_launch", "algorithmic_bytes_per_launch"):
+                    out[parts[0]] = int(float(parts[1]))
     except OSError:
-        pass
-    return None
+        return None
+    return out or None
 
 
 def case_bytes_flops(m, k, n, fmt="fp8", gs=128):
@@ -181,6 +194,7 @@ class ClockSampler:
 
 
 def cpu_sample_cases(seed=0):
+    """The same 42 linears as the GPU step (full M, up to 8192 rows)."""
     from oracle import nsq_oracle as O
     rng = np.random.default_rng(seed)
     cases = []
@@ -188,9 +202,8 @@ def cpu_sample_cases(seed=0):
         w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
         codes, scale = O.fp8_quantize(w)
         for m in MS:
-            mm = min(m, CPU_SAMPLE_MAX_M)
-            x = O.bf16_round(rng.standard_normal((mm, k)).astype(np.float32))
-            cases.append((codes, scale, x, 2 * mm * n * k))
+            x = O.bf16_round(rng.standard_normal((m, k)).astype(np.float32))
+            cases.append((codes, scale, x, 2 * m * n * k))
     return cases
 
 
@@ -200,32 +213,30 @@ def cpu_oracle_step(cases):
         O.fp8_linear(x, codes, scale)
 
 
-def cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        info = threadpool_info()
-        if info:
-            return max(int(i.get("num_threads", 1)) for i in info)
-    except Exception:
-        pass
+def host_cores():
     return len(os.sched_getaffinity(0))
 
 
 def run_cpu_baseline(steps, warmup):
-    cases = cpu_sample_cases()
-    flops = sum(c[3] for c in cases)
-    for _ in range(warmup):
-        cpu_oracle_step(cases)
-    t = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        cpu_oracle_step(cases)
-        t.append(time.perf_counter() - t0)
+    """The oracle on every host core the process may use (threadpoolctl sets
+    the BLAS pool explicitly: under torchrun it would otherwise start at 1)."""
+    from threadpoolctl import threadpool_limits
+    cores = host_cores()
+    with threadpool_limits(limits=cores):
+        cases = cpu_sample_cases()
+        flops = sum(c[3] for c in cases)
+        for _ in range(warmup):
+            cpu_oracle_step(cases)
+        t = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            cpu_oracle_step(cases)
+            t.append(time.perf_counter() - t0)
     sec = statistics.median(t)
-    return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"all 42 sweep linears with M capped at {CPU_SAMPLE_MAX_M} rows "
-                      f"({flops / 1e9:.1f} GFLOP), numpy fp32 dequant+matmul, median of {steps}",
-            "ms_per_step": sec * 1e3}
+    return {"value": flops / sec / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"all 42 sweep linears at full M ({flops / 1e9:.1f} GFLOP, the GPU step's work), "
+                      f"numpy fp32 dequant+matmul, median of {steps}",
+            "same_config": True, "ms_per_step": sec * 1e3}
 
 
 # ---------------------------------------------------------------------------
@@ -347,6 +358,11 @@ def run_ours(args):
     sampler.stop()
     flops_total = sum(2 * c["m"] * c["n"] * c["k"] for c in cases)  # full (unsharded) sweep work
     value = flops_total / (ms_step * 1e-3) / 1e12
+    # the timed graph's own outputs (last replay) against the unsharded layer
+    parity = check_parity(torch, dist, ops, cases, rank, world, device)
+    tp_breakdown = None
+    if world > 1:
+        tp_breakdown = time_tp_breakdown(cases, capture, time_graph, args, ms_step)
 
     # --- dominant kernel: all prefill-GEMM launches (M > 64) as one graph ---
     pre = [c for c in cases if c["m"] > 64]
@@ -363,11 +379,13 @@ def run_ours(args):
     roofline = {"kernel": "prefill GEMMs (tcgen05 kind::f16; dequantised weight as the TMEM operand: paired-CTA and one-CTA; split-K cluster)",
                 "bound": "tensor", "achieved": round(ach, 2), "peak": bf16_peak, "unit": "TFLOP/s",
                 "frac": round(ach / bf16_peak, 4), "peak_source": f"{peak_src} bf16 dense (burst)",
-                "launches_per_step": len(pre_k),
-                "traffic": profiled_traffic("sweep_prefill") if world == 1 else None,
-                "algorithmic_bytes_per_launch": int(sum(case_bytes_flops(c["m"], c["ks"], c["ns"])[0]
-                                                        for c in pre_k) / len(pre_k)),
-                "traffic_source": "ncu capture, mean per launch of the same 21 linears"}
+                "launches_per_step": len(pre_k)}
+    tr = profiled_traffic() if world == 1 else None
+    roofline.update({
+        "traffic": tr.get("traffic_bytes_per_launch") if tr else None,
+        "traffic_algorithmic_bytes": tr.get("algorithmic_bytes_per_launch") if tr else None,
+        "traffic_case": "one launch of the sweep's top prefill linear (FP8 down 4864->896, M=8192), "
+                        "ncu dram__bytes_read.sum + dram__bytes_write.sum, one-kernel capture"})
     # decode kernel (M <= 64) class, for context
     dec = [dict(c, row=False) for c in cases if c["m"] <= 64]
     g_dec = capture(dec)
@@ -379,7 +397,6 @@ def run_ours(args):
                    "peak": hbm_peak, "unit": "GB/s",
                    "frac": round(bytes_dec / (ms_dec * 1e-3) / 1e9 / hbm_peak, 4),
                    "launches_per_step": len(dec), "us_per_launch": round(ms_dec * 1e3 / len(dec), 2),
-                   "traffic": profiled_traffic("decode") if world == 1 else None,
                    "algorithmic_bytes_per_launch": int(bytes_dec / len(dec))}
     del g_all, g_pre, g_dec
 
@@ -465,17 +482,84 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "linears_per_step": len(cases), "weights": "fp8 e4m3, per-tensor scale",
-                       "activations": "bf16 N(0,1)", "parallelism": f"tp{world}",
-                       "l2": "flushed between timed steps (256 MiB write)", "timing": "CUDA graph replay, CUDA events",
-                       "pdl": not args.no_pdl},
+            "config": sweep_config(world),
             "roofline": roofline, "decode_kernel": decode_line, "awq_config0": awq, "cpu_baseline": cpu,
-            "e2e": e2e, "gpu_launches": len(cases) * args.steps, "clocks": clocks,
+            "e2e": e2e, "gpu_launches": len(cases) * args.steps, "clocks": clocks, "parity": parity,
         }
+        if tp_breakdown is not None:
+            out["tp_breakdown"] = tp_breakdown
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return out
+
+
+def check_parity(torch, dist, ops, cases, rank, world, device):
+    """Max relative Frobenius error of the step's outputs against an fp32 product
+    of the bit-exact dequantised weight (quantization.py:49-52). Under TP the
+    shards of x, the weight codes and y are gathered first (column-parallel y
+    along N; row-parallel y is already summed by the all-reduce), and rank 0
+    checks them against the unsharded layer."""
+    def gather(t, dim):
+        if world == 1:
+            return t
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous())
+        return torch.cat(parts, dim=dim)
+
+    worst, worst_name = 0.0, None
+    one = torch.ones((), device=device)
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for c in cases:
+            codes8 = c["codes"].view(torch.uint8)
+            if c["row"]:
+                x, codes, y = gather(c["x"], 1), gather(codes8, 1), c["y"]
+            else:
+                x, codes, y = c["x"], gather(codes8, 0), gather(c["y"], 1)
+            if rank != 0:
+                continue
+            w = ops.fp8_dequant(codes.view(torch.float8_e4m3fn), one, torch.float16).float() * c["scale"]
+            ref = x.float() @ w.T
+            err = ((y.float() - ref).norm() / ref.norm()).item()
+            if err > worst:
+                worst, worst_name = err, f'{c["name"]} M={c["m"]}'
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+    if rank != 0:
+        return None
+    return {"max_rel_fro": float(f"{worst:.3e}"), "worst_case": worst_name, "cases": len(cases),
+            "tol": PARITY_TOL, "pass": worst <= PARITY_TOL,
+            "reference": "fp32 product of the bit-exact dequantised weight (TF32 off)"
+                         + (", TP shards gathered to the unsharded layer" if world > 1 else "")}
+
+
+def time_tp_breakdown(cases, capture, time_graph, args, ms_step):
+    """Where a TP step's time goes: the 42 linears alone (no collective) and
+    the 12 row-parallel all-reduces alone, each as its own graph."""
+    import torch.distributed as dist
+    lin = [dict(c, row=False) for c in cases]
+    g_lin = capture(lin)
+    ms_lin = time_graph(g_lin, args.steps, args.warmup)
+    del g_lin
+    rows = [c for c in cases if c["row"]]
+    import torch
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for c in rows:
+            dist.all_reduce(c["y"])
+    torch.cuda.synchronize()
+    g_ar = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_ar, stream=stream):
+        for c in rows:
+            dist.all_reduce(c["y"])
+    torch.cuda.synchronize()
+    ms_ar = time_graph(g_ar, args.steps, args.warmup)
+    del g_ar
+    return {"step_ms": round(ms_step, 4), "linears_only_ms": round(ms_lin, 4), "allreduce_only_ms": round(ms_ar, 4),
+            "allreduces_per_step": len(rows),
+            "allreduce_bytes_per_step": int(sum(c["y"].numel() * 2 for c in rows))}
 
 
 def bench_awq_config0(torch, ops, device, args, peaks, peak_src, flush):
@@ -535,9 +619,9 @@ def run_reference(args):
         "WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 2),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": WORKLOAD, "parallelism": "cpu", "sample": r["sample"]},
+        "config": sweep_config(int(os.environ.get("WORLD_SIZE", "1"))),
         "cpu_baseline": {"value": round(r["value"], 5), "unit": "TFLOP/s", "cores": r["cores"], "kind": "port",
-                         "sample": r["sample"]},
+                         "sample": r["sample"], "same_config": True},
         "e2e": {"value": round(r["value"], 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -556,12 +640,12 @@ def run_ncu_case(name):
         x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
         for _ in range(3):
             ops.fp8_linear(x, codes, scale)
-    elif name in ("decode", "sweep_prefill"):
-        for _, k, n in SHAPES:
-            codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
-            for m in [mm for mm in MS if (mm <= 64) == (name == "decode")]:
-                x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
-                ops.fp8_linear(x, codes, scale)
+    elif name == "down8192":
+        m, k, n = 8192, 4864, 896
+        codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        for _ in range(3):
+            ops.fp8_linear(x, codes, scale)
     elif name == "awq0":
         m, k, n, gs = 16, 896, 9728, 128
         for _ in range(4):
@@ -586,7 +670,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle leg")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
-    ap.add_argument("--ncu-case", choices=["prefill", "sweep_prefill", "decode", "awq0"], default=None,
+    ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0"], default=None,
                     help="run a small case of one kernel class for a profiler capture, then exit")
     args = ap.parse_args()
     if args.ncu_case:

@@ -138,6 +138,22 @@ int nsq_fp8_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* 
 int nsq_fp8_quantize_noalloc(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* weight_fp8,
                              float* weight_scale, void* stream);
 
+/* Limit, in nanoseconds, of every bounded device-side wait that reports to the
+ * status word (0 restores the default of 2 s; nsq_device_status_reset also
+ * restores it). The wind-down waits that let in-flight copies land after a
+ * failure always use the default. No counterpart in the reference (its path
+ * has no device-side waits); used by the failure-path tests. */
+int nsq_set_wait_limit_ns(uint64_t ns);
+
+/* Failure-path test hook, off by default; returns the previous setting. While
+ * on, the multi-wave decode kernel (the AWQ/FP8 linear with M <= 64 when it is
+ * chosen, e.g. M = 16, K = 896, N = 9728) never requests the first weight box
+ * of its first row group, so that group's bounded wait runs out: the kernel
+ * records NSQ_EDEVICE_TIMEOUT (tag 1) in the status word, lets every copy it
+ * did request land, and returns. Its output is then undefined. No counterpart
+ * in the reference. Not for production use. */
+int nsq_test_withhold_weight_load(int enable);
+
 /* Opt in (1) or out (0, default) of programmatic dependent launch for the
  * linear kernels: with it on, a linear starts streaming its weights while the
  * previous kernel on the stream drains. Only valid when no kernel earlier on

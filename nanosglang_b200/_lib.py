@@ -52,6 +52,8 @@ SIGNATURES = {
                                  c_void_p]),
     "nsq_fp8_quantize_noalloc": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "nsq_set_pdl": (c_int, [c_int]),
+    "nsq_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
+    "nsq_test_withhold_weight_load": (c_int, [c_int]),
 }
 
 _lib = None
@@ -109,4 +111,15 @@ def device_status():
 
 
 def device_status_reset() -> None:
+    """Clear the device status word (also restores the default wait limit)."""
     check(load().nsq_device_status_reset(), "nsq_device_status_reset")
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Limit of every bounded device wait that reports to the status word (0 = the 2 s default)."""
+    check(load().nsq_set_wait_limit_ns(int(ns)), "nsq_set_wait_limit_ns")
+
+
+def withhold_weight_load_for_test(enable: bool) -> bool:
+    """Failure-path test hook (see include/nsq.h); returns the previous setting."""
+    return bool(load().nsq_test_withhold_weight_load(1 if enable else 0))

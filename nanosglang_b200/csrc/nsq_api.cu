@@ -5,8 +5,9 @@
 // failure modes where it has them (e.g. in_features % 8 != 0 raises in
 // AWQLinear._dequantize, quantization.py:134-137); everything else the
 // kernels need (alignment, K multiples for TMA) is reported as an error code.
-#include <mutex>
 #include <atomic>
+#include <cstddef>
+#include <mutex>
 
 #include "nsq_common.cuh"
 #include "nsq_internal.h"
@@ -19,12 +20,14 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-int g_sms[kMaxDevices] = {0};
-int g_arch_ok[kMaxDevices] = {0};  // 0 unknown, 1 ok, -1 not sm_100
-DevStatus* g_status_ptr[kMaxDevices] = {nullptr};
+// per-device caches, written once under g_mu and read without it
+std::atomic<int> g_sms[kMaxDevices];
+std::atomic<int> g_arch_ok[kMaxDevices];  // 0 unknown, 1 ok, -1 not sm_100
+std::atomic<DevStatus*> g_status_ptr[kMaxDevices];
 std::atomic<int> g_pdl{0};
+std::atomic<int> g_withhold{0};  // failure-path test hook (nsq_test_withhold_weight_load)
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::atomic<PFN_cuTensorMapEncodeTiled_v12000> g_encode{nullptr};
 
 int current_device() {
   int d = 0;
@@ -36,8 +39,9 @@ int current_device() {
 int check_device() {
   const int d = current_device();
   if (d < 0) return NSQ_ECUDA;
-  if (g_arch_ok[d] == 1) return NSQ_OK;
-  if (g_arch_ok[d] == -1) return NSQ_ENOTSUP;
+  const int known = g_arch_ok[d].load(std::memory_order_acquire);
+  if (known == 1) return NSQ_OK;
+  if (known == -1) return NSQ_ENOTSUP;
   std::lock_guard<std::mutex> lk(g_mu);
   int major = 0, minor = 0, sms = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d) != cudaSuccess ||
@@ -45,9 +49,10 @@ int check_device() {
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess) {
     return NSQ_ECUDA;
   }
-  g_sms[d] = sms;
-  g_arch_ok[d] = (major == 10 && minor == 0) ? 1 : -1;
-  return g_arch_ok[d] == 1 ? NSQ_OK : NSQ_ENOTSUP;
+  g_sms[d].store(sms, std::memory_order_relaxed);
+  const int arch = (major == 10 && minor == 0) ? 1 : -1;
+  g_arch_ok[d].store(arch, std::memory_order_release);
+  return arch == 1 ? NSQ_OK : NSQ_ENOTSUP;
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -64,33 +69,41 @@ constexpr int64_t kIntMax = 0x7FFFFFFF;
 int num_sms() {
   const int d = current_device();
   if (d < 0) return 148;
-  if (g_sms[d] == 0) check_device();
-  return g_sms[d] > 0 ? g_sms[d] : 148;
+  if (g_sms[d].load(std::memory_order_acquire) == 0) check_device();
+  const int sms = g_sms[d].load(std::memory_order_acquire);
+  return sms > 0 ? sms : 148;
 }
 
 DevStatus* device_status_ptr() {
   const int d = current_device();
   if (d < 0) return nullptr;
-  if (g_status_ptr[d] != nullptr) return g_status_ptr[d];
+  DevStatus* cached = g_status_ptr[d].load(std::memory_order_acquire);
+  if (cached != nullptr) return cached;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_status_ptr[d] == nullptr) {
+  cached = g_status_ptr[d].load(std::memory_order_relaxed);
+  if (cached == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
-    g_status_ptr[d] = static_cast<DevStatus*>(p);
+    cached = static_cast<DevStatus*>(p);
+    g_status_ptr[d].store(cached, std::memory_order_release);
   }
-  return g_status_ptr[d];
+  return cached;
 }
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
+bool test_withhold() { return g_withhold.load(std::memory_order_relaxed) != 0; }
 
 int device_ready() { return check_device(); }
 
 CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
                               uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
-  if (g_encode == nullptr) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = g_encode.load(std::memory_order_acquire);
+  if (encode == nullptr) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (g_encode == nullptr) {
+    encode = g_encode.load(std::memory_order_relaxed);
+    if (encode == nullptr) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
       if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
@@ -98,14 +111,15 @@ CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void*
           q != cudaDriverEntryPointSuccess || fn == nullptr) {
         return CUDA_ERROR_NOT_FOUND;
       }
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+      g_encode.store(encode, std::memory_order_release);
     }
   }
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_stride_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  return g_encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  return encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
@@ -149,6 +163,17 @@ int nsq_device_status_reset(void) {
   return cudaMemcpyToSymbol(g_device_status, &st, sizeof(st)) == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
 }
 
+int nsq_set_wait_limit_ns(uint64_t ns) {
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  const unsigned long long v = ns;
+  return cudaMemcpyToSymbol(g_device_status, &v, sizeof(v), offsetof(DevStatus, wait_limit_ns)) == cudaSuccess
+             ? NSQ_OK
+             : NSQ_ECUDA;
+}
+
+int nsq_test_withhold_weight_load(int enable) { return g_withhold.exchange(enable ? 1 : 0); }
+
 int nsq_awq_dequant(const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
                     uint16_t* w_out, int64_t N, int64_t K, int64_t group_size, void* stream) {
   if (N < 0 || K <= 0 || group_size <= 0 || K % 8 != 0) return NSQ_EINVAL;
@@ -165,6 +190,7 @@ int nsq_awq_dequant(const int32_t* qweight, const uint16_t* scales, const uint16
 int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* w_out,
                     int out_dtype, int64_t N, int64_t K, void* stream) {
   if (N < 0 || K <= 0 || !valid_act_dtype(out_dtype)) return NSQ_EINVAL;
+  if (N > INT64_MAX / K) return NSQ_EINVAL;
   if (N == 0) return NSQ_OK;
   if (!weight_fp8 || !weight_scale || !w_out) return NSQ_EINVAL;
   if (!aligned16(weight_fp8) || !aligned16(w_out)) return NSQ_EALIGN;
@@ -295,6 +321,7 @@ size_t nsq_fp8_quantize_workspace_size(int64_t N, int64_t K) {
 int nsq_fp8_quantize(const void* w, int w_dtype, int64_t N, int64_t K, uint8_t* weight_fp8,
                      float* weight_scale, void* workspace, size_t workspace_bytes, void* stream) {
   if (N < 0 || K < 0) return NSQ_EINVAL;
+  if (K > 0 && N > INT64_MAX / K) return NSQ_EINVAL;  // N * K must not overflow
   if (!(w_dtype == NSQ_DTYPE_F16 || w_dtype == NSQ_DTYPE_BF16 || w_dtype == NSQ_DTYPE_F32)) {
     return NSQ_EINVAL;
   }

@@ -25,10 +25,13 @@ struct DevStatus {
   unsigned int where;  // which wait gave up (kernel-specific tag)
   unsigned int block;  // linear block index that gave up
   unsigned int pad;
+  unsigned long long wait_limit_ns;  // limit of the waits that report here; 0 = default
 };
 
-// Upper bound for any single wait on an mbarrier (nanoseconds). Normal waits
-// last microseconds; reaching this means a protocol bug, not a slow GPU.
+// Default upper bound for any single wait on an mbarrier (nanoseconds).
+// Normal waits last microseconds; reaching this means a protocol bug, not a
+// slow GPU. Waits that report to the status word use its wait_limit_ns when
+// set; the wind-down waits (no status word) always use this bound.
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -79,16 +82,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait. Returns false (after recording the failure and raising the
-// CTA-wide abort flag) if the phase does not complete within kWaitTimeoutNs
+// CTA-wide abort flag) if the phase does not complete within the limit
 // or if another thread of the CTA already aborted.
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, DevStatus* st,
                                             uint32_t where, volatile int* abort_flag) {
   const unsigned long long t0 = globaltimer_ns();
+  unsigned long long limit = kWaitTimeoutNs;
+  if (st != nullptr) {
+    const unsigned long long l = *reinterpret_cast<volatile unsigned long long*>(&st->wait_limit_ns);
+    if (l != 0ull) limit = l;
+  }
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      if (globaltimer_ns() - t0 > limit) {
         if (st != nullptr && atomicCAS(&st->code, 0u, (unsigned)NSQ_EDEVICE_TIMEOUT) == 0u) {
           st->where = where;
           st->block = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);

@@ -85,6 +85,7 @@ struct DecodeParams {
   int ppc;      // pieces per x staging chunk
   int xrs;      // bytes per token row of an x buffer (ppc * piece * 2)
   int bias_dtype;
+  int withhold;  // test hook: row group 0 of every CTA skips its first weight box
   int off_x, off_xsum, off_sz, off_red, off_redk, off_bar, off_abort;
 };
 
@@ -305,7 +306,10 @@ __global__ void __launch_bounds__(kMaxThreads, 2) decode_linear_kernel(
     for (int sl = 0; sl < nslab_used; ++sl) mbar_init(&sbar[sl], 1);
     fence_proxy_async_smem();
     const int kbytes = FMT == 0 ? k_begin / 2 : k_begin;  // byte offset of the slice in a row
-    for (int sl = 0; sl < nslab_used; ++sl) {
+    // (test hook: with p.withhold, row group 0 never requests its first box,
+    // so its waits run out and the CTA winds down through the abort path;
+    // nothing is in flight for the box that was never requested)
+    for (int sl = (p.withhold && rg == 0) ? 1 : 0; sl < nslab_used; ++sl) {
       mbar_arrive_expect_tx(&sbar[sl], 16 * p.slab_row);
       tma_load_2d(smem + rg * group_bytes + sl * 16 * p.slab_row, &wmap, &sbar[sl],
                   (kbytes + sl * p.slab_row) / 4, n0 + 16 * rg);
@@ -678,6 +682,7 @@ int run_decode_linear(const LinearArgs& a, cudaStream_t stream) {
   p.ppc = pl.ppc;
   p.xrs = pl.xrs;
   p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
+  p.withhold = test_withhold() ? 1 : 0;
   p.off_x = pl.off_x;
   p.off_xsum = pl.off_xsum;
   p.off_sz = pl.off_sz;

@@ -746,7 +746,10 @@ int max_active_clusters(int s) {
   const int cached = cache[dev][slot].load();
   if (cached > 0) return cached - 1;
   auto kern = decode_wave_kernel<1, true, 1>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(s, 1, 1);
   cfg.blockDim = dim3(WaveThreads<1, 1>::kThreads, 1, 1);

@@ -14,6 +14,7 @@ int num_sms();                  // SM count of the current device (cached per de
 int device_ready();             // NSQ_OK if the current device is sm_100, else an NSQ_E* code
 DevStatus* device_status_ptr(); // device address of this device's status word (lazily set up)
 bool pdl_enabled();
+bool test_withhold();  // failure-path test hook: the multi-wave decode kernel skips one weight load
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (libnsq does
 // not link libcuda directly, so it also loads on machines without a driver).

@@ -20,6 +20,7 @@
 // The device address of the array is looked up once per device with that
 // device current (cudaGetSymbolAddress); the first call on a device does this
 // set-up, so make that first call before any stream capture begins.
+#include <atomic>
 #include <mutex>
 
 #include "nsq_common.cuh"
@@ -34,21 +35,24 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 constexpr int kMaxDev = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kMaxDev] = {nullptr};
+std::atomic<void*> g_noalloc_addr[kMaxDev];  // zero-initialised (static storage)
 
 // Device address of g_noalloc_scratch on the current device (set up once per
 // device), or nullptr if the runtime refuses.
 void* noalloc_scratch_on_current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
-  if (g_noalloc_addr[dev] != nullptr) return g_noalloc_addr[dev];
+  void* cached = g_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (cached != nullptr) return cached;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  cached = g_noalloc_addr[dev].load(std::memory_order_relaxed);
+  if (cached == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
-    g_noalloc_addr[dev] = p;
+    g_noalloc_addr[dev].store(p, std::memory_order_release);
+    cached = p;
   }
-  return g_noalloc_addr[dev];
+  return cached;
 }
 
 }  // namespace
@@ -60,6 +64,7 @@ using namespace nsq;
 extern "C" int nsq_fp8_quantize_noalloc(const void* w, int w_dtype, int64_t N, int64_t K,
                                         uint8_t* weight_fp8, float* weight_scale, void* stream) {
   if (N < 0 || K < 0) return NSQ_EINVAL;
+  if (K > 0 && N > INT64_MAX / K) return NSQ_EINVAL;  // N * K must not overflow
   if (!(w_dtype == NSQ_DTYPE_F16 || w_dtype == NSQ_DTYPE_BF16 || w_dtype == NSQ_DTYPE_F32)) {
     return NSQ_EINVAL;
   }

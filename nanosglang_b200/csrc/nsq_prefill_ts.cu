@@ -543,14 +543,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         if (etid == 0) mbar_wait(peers_received, 0, p.status, 61, nullptr);
       }
       tc_fence_before();  // the TMEM reads above precede the deallocation
-    } else if (warp == kWarpEpi0 && lane == 0) {
-      // This rank gave up (a bounded wait ran out). The other ranks may still
-      // arrive on its barriers and copy into its shared memory: let those
-      // land (bounded) before the CTA can exit.
+    }
+    if (warp == kWarpEpi0 && lane == 0) {
+      // Every way out of the exchange passes here. After a wait that ran out
+      // (in the main loop or in the exchange above) the other ranks may still
+      // arrive on this CTA's barriers and copy into its shared memory: let
+      // those land (bounded) before the CTA can leave. When the exchange
+      // completed, all three phases are already complete and these waits
+      // return at once.
       mbar_wait(peers_free, 0, nullptr, 0, nullptr);
       mbar_wait(recv, 0, nullptr, 0, nullptr);
+      mbar_wait(peers_received, 0, nullptr, 0, nullptr);
     }
     if (warp < kWarpEpi0) cluster_wait_acq();
+    // No CTA of the cluster exits while another one may still address its
+    // shared memory: every rank reaches this barrier (all waits above are
+    // bounded) only after its own remote operations were issued and the
+    // ones aimed at it landed or were given up on.
+    cluster_arrive_rel();
+    cluster_wait_acq();
   }
 
   pdl_launch_dependents();

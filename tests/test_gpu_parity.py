@@ -333,6 +333,23 @@ def test_fp8_linear_vs_reference_forward_golden():
         assert O.rel_fro(_to_np(y), O.from_bf16_bits(d[f"c{ci}_y"])) <= GEMM_TOL, ci
 
 
+@pytest.mark.parametrize("kn", QWEN05_SHAPES)
+def test_fp8_linear_config1_m8192_oracle(kn):
+    """The benchmarked M = 8192 launches of config 1 (q/o 896->896, k/v 896->128,
+    gate/up 896->4864, down 4864->896) against the fp32 oracle."""
+    k, n = kn
+    err = _fp8_case(8192, n, k, torch.bfloat16, bias=False, seed=8192 + 3 * n + k)
+    assert err <= GEMM_TOL, err
+
+
+@pytest.mark.parametrize("kn", [(896, 4864), (4864, 896)])
+def test_awq_linear_m8192_oracle(kn):
+    """AWQ W4A16 at M = 8192 on the gate/up and down shapes against the fp32 oracle."""
+    k, n = kn
+    err = _awq_case(8192, n, k, 128, torch.bfloat16, bias=False, zm="int", seed=8192 + n)
+    assert err <= GEMM_TOL, err
+
+
 def test_fp8_linear_full_size_property_m8192():
     """Config-1 largest case, checked against an fp32 torch reference built from
     the bit-exact dequantised weight (size-independent property check)."""
