@@ -468,6 +468,12 @@ def run_ours(args):
     if world == 1:
         awq = bench_awq_config0(torch, ops, device, args, peaks, peak_src, flush)
 
+    # --- model level: configs 2 and 3 (tok/s) -------------------------------
+    tok_s = None
+    if not args.no_model:
+        tok_s = {"config2": bench_config2_tok_s(torch, dist, device, rank, world, args),
+                 "config3": bench_config3_tok_s(torch, dist, device, rank, world, args)}
+
     code, where, block = _lib.device_status()
     if code != 0:
         raise RuntimeError(f"device status {code} (tag {where}, block {block})")
@@ -485,6 +491,7 @@ def run_ours(args):
             "config": sweep_config(world),
             "roofline": roofline, "decode_kernel": decode_line, "awq_config0": awq, "cpu_baseline": cpu,
             "e2e": e2e, "gpu_launches": len(cases) * args.steps, "clocks": clocks, "parity": parity,
+            "tok_s": tok_s,
         }
         if tp_breakdown is not None:
             out["tp_breakdown"] = tp_breakdown
@@ -560,6 +567,112 @@ def time_tp_breakdown(cases, capture, time_graph, args, ms_step):
     return {"step_ms": round(ms_step, 4), "linears_only_ms": round(ms_lin, 4), "allreduce_only_ms": round(ms_ar, 4),
             "allreduces_per_step": len(rows),
             "allreduce_bytes_per_step": int(sum(c["y"].numel() * 2 for c in rows))}
+
+
+def bench_config2_tok_s(torch, dist, device, rank, world, args):
+    """Qwen2.5-0.5B, AWQ int4 on every projection (config-0
+    distributions, random init), 32 requests, prompts U[100, 512], outputs
+    U[64, 128], greedy, all requests admitted at once; output tokens / wall
+    clock through the harness engine (packed prefill + CUDA-graph decode
+    steps), prompts up from pinned host memory and tokens back inside the
+    timed region. At N GPUs: N independent replicas, requests split
+    round-robin (the 14 query / 2 KV heads do not shard 4 or 8 ways), tokens
+    summed, time = the slowest replica."""
+    from harness import engine as E
+    from harness import model as H
+    cfg = H.QWEN2_5_0_5B
+    model = H.build_model(cfg, device=device, dtype=torch.bfloat16)
+    H.quantize_projections_awq(model)
+    H.init_awq(model, 2)
+    prompts, outs = E.make_workload(32, 100, 512, 64, 128, cfg.vocab_size, seed=0)
+    mine = list(range(rank, len(prompts), world))
+    ps, os_ = [prompts[i] for i in mine], [outs[i] for i in mine]
+    eng = E.DecodeEngine(model, max_slots=len(ps), max_len=512 + 128 + 8, max_steps=128)
+    eng.capture()
+    step_ms = E.time_decode_step(eng, len(ps))
+    E.run_workload(eng, ps, os_)  # warm-up (allocator, prefill shapes)
+    runs = []
+    for _ in range(3):
+        if world > 1:
+            dist.barrier()
+        _, info = E.run_workload(eng, ps, os_)
+        el = info["elapsed_s"]
+        if world > 1:
+            t = torch.tensor([el], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            el = float(t.item())
+        runs.append(el)
+    el = statistics.median(runs)
+    total_out = sum(outs)
+    del eng, model
+    torch.cuda.empty_cache()
+    return {"workload": "config 2: Qwen2.5-0.5B AWQ int4 (all projections), 32 requests, prompt U[100,512], "
+                        "output U[64,128], greedy, bf16 activations", "tok_s": round(total_out / el, 1),
+            "unit": "output tokens/s (wall clock)", "elapsed_s": round(el, 4), "output_tokens": total_out,
+            "prompt_tokens": sum(len(p) for p in prompts), "replicas": world,
+            "decode_step_ms": round(step_ms, 4), "decode_step_batch": len(ps),
+            "method": "packed prefill + one CUDA-graph replay per decode step (harness engine); "
+                      "median of 3 runs after one warm-up"}
+
+
+def bench_config3_tok_s(torch, dist, device, rank, world, args):
+    """Llama-3-8B-shaped decoder, AWQ int4 on every
+    projection (random init), 64 decode streams at context 2048, tensor
+    parallel over the N ranks (q/k/v/gate/up column-parallel, o/down
+    row-parallel + NCCL all-reduce, inside the captured decode graph).
+    The caches hold 2048 positions of random keys/values (the prefill is not
+    part of this figure); tok/s = 64 x steps / device time of the steps,
+    max over ranks."""
+    from harness import engine as E
+    from harness import model as H
+    from nanosglang_b200 import tensor_parallel as TP
+    cfg = H.LLAMA3_8B
+    streams, ctx, steps = 64, 2048, 16
+    model = H.build_model(cfg, device=device, dtype=torch.bfloat16)
+    H.quantize_projections_awq(model)
+    H.init_awq(model, 3)
+    if world > 1:
+        TP.tensor_parallel_model(model, world, rank)
+    eng = E.DecodeEngine(model, max_slots=streams, max_len=ctx + steps + 8, max_steps=steps + 4)
+    g = torch.Generator(device=device).manual_seed(4 + rank)
+    for kc, vc in eng.caches:
+        kc.normal_(generator=g)
+        vc.normal_(generator=g)
+    eng.capture([streams])
+    eng.tokens.copy_(torch.randint(0, cfg.vocab_size, (streams,), generator=g, device=device))
+    gph = eng.graphs[streams]
+
+    def run(n):
+        eng.positions.fill_(ctx)
+        eng.step.zero_()
+        for _ in range(n):
+            gph.replay()
+
+    run(3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eng.positions.fill_(ctx)
+    eng.step.zero_()
+    s_ev.record()
+    for _ in range(steps):
+        gph.replay()
+    e_ev.record()
+    torch.cuda.synchronize()
+    ms = s_ev.elapsed_time(e_ev) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    wbytes = sum(b.numel() * b.element_size() for n, b in model.named_buffers()
+                 if n.endswith(("qweight", "scales", "zeros")))
+    del gph, eng, model
+    torch.cuda.empty_cache()
+    return {"workload": "config 3: Llama-3-8B AWQ int4, 64 streams at context 2048, bf16 activations",
+            "tok_s": round(streams / (ms * 1e-3), 1), "unit": "tokens/s (device time of decode steps)",
+            "ms_per_step": round(ms, 4), "tp": world, "awq_weight_bytes_per_rank": int(wbytes),
+            "method": f"{steps} replays of the batch-64 decode-step graph, max over ranks"}
 
 
 def bench_awq_config0(torch, ops, device, args, peaks, peak_src, flush):
@@ -670,6 +783,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle leg")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--no-model", action="store_true", help="skip the model-level tok/s legs (configs 2 and 3)")
     ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0"], default=None,
                     help="run a small case of one kernel class for a profiler capture, then exit")
     args = ap.parse_args()
