@@ -164,8 +164,12 @@ class Attention(nn.Module):
         rows = torch.arange(bs, device=hidden_states.device)
         k_cache[rows, :, positions, :] = k
         v_cache[rows, :, positions, :] = v
-        out = F.scaled_dot_product_attention(q.unsqueeze(2), k_cache[:bs], v_cache[:bs], attn_mask=mask,
-                                             scale=1.0 / math.sqrt(self.head_dim), enable_gqa=nh != nkv)
+        # grouped-query decode as multi-query attention: the nh / nkv query
+        # heads that share a KV head take the place of query positions, so
+        # every KV head is read once and the masked kernel needs no GQA support
+        qg = q.view(bs, nkv, nh // nkv, self.head_dim)
+        out = F.scaled_dot_product_attention(qg, k_cache[:bs], v_cache[:bs], attn_mask=mask,
+                                             scale=1.0 / math.sqrt(self.head_dim))
         return self.o_proj(out.reshape(bs, nh * self.head_dim))
 
     def forward_prefill(self, hidden_states, cos, sin, positions, k_cache, v_cache, slot):
