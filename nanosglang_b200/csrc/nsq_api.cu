@@ -212,6 +212,15 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     //     single-wave kernel;
     //   * otherwise the multi-wave kernel; the tensor-core GEMM when no
     //     decode plan fits.
+    // 33..64 tokens on a large weight: the tcgen05 kernel with the dequantised
+    // weight tile in tensor memory beats the mma.sync kernels, whose tensor
+    // work grows with the token count (B200, CUDA-graph chains, AWQ at
+    // M = 64: Llama-3-8B gate 140 -> 47 us, down 146 -> 47 us, q 52 -> 18 us,
+    // 896 -> 9728 19.5 -> 12.6 us; 4096 -> 1024 stays faster on mma.sync)
+    if (a.M > 32 && (int64_t)a.K * a.N >= ((int64_t)1 << 23)) {
+      const TsPlan tp = prefill_ts_plan(a.fmt, a.M, a.K, a.N);
+      if (tp.tokens_per_tile > 0) return run_prefill_ts_linear(a, tp, stream);
+    }
     const int ctas = decode_linear_ctas(a);
     if (ctas < 0 || ctas > 2 * num_sms()) {
       const int rc = run_decode_stream_linear(a, stream);

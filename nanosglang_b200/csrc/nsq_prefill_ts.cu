@@ -673,16 +673,18 @@ TsPlan prefill_ts_plan(int fmt, int64_t M, int64_t K, int64_t N) {
   // on B200 over the Qwen2.5-0.5B and Llama-3-8B shapes at M = 128 / 1024. At
   // least 2 k-blocks per CTA.
   TsPlan best{0, 1};
-  if (M <= kDecodeMaxM) return best;
+  // decode-sized batches (M <= 64) take the one-CTA kernel with 64-token tiles
+  const bool decode = M <= kDecodeMaxM;
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
   const int sms = num_sms();
-  if (M * N > ((int64_t)1 << 20) && pair_tiles * 4 > sms) return best;
+  if (!decode && M * N > ((int64_t)1 << 20) && pair_tiles * 4 > sms) return best;
   const int64_t kb = (K + BK - 1) / BK;
   const int64_t wt = (N + BW - 1) / BW;
   const double c = fmt == 0 ? 0.52 : 0.28;
   const double f = fmt == 0 ? 6.2 : 5.7;
   double best_cost = 0.0;
   for (int bt : {64, 128}) {
+    if (decode && bt == 128) break;
     const int64_t units = wt * ((M + bt - 1) / bt);
     for (int ks = 1; ks <= bt / kXChunk; ks *= 2) {
       if (ks > 1 && (units * ks > sms || (kb + ks - 1) / ks < 2)) break;
@@ -695,7 +697,9 @@ TsPlan prefill_ts_plan(int fmt, int64_t M, int64_t K, int64_t N) {
       }
     }
   }
-  if (fmt == 0 && pair_tiles * 2 <= sms && 4.5 + 1.1 * (double)((kb + 1) / 2) < best_cost) return TsPlan{0, 1};
+  if (!decode && fmt == 0 && pair_tiles * 2 <= sms && 4.5 + 1.1 * (double)((kb + 1) / 2) < best_cost) {
+    return TsPlan{0, 1};
+  }
   return best;
 }
 

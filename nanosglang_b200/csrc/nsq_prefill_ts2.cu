@@ -102,8 +102,23 @@ struct Ts2Params {
   int group_size, G;
   int bias_dtype;
   int num_w_tiles, num_t_tiles, num_kb;  // w tiles of 256 rows, t tiles of 256 tokens
+  int wt_fast;  // unit order: weight tile fastest (1) or token tile fastest (0)
   int num_st;                            // stages per tile: ceil(num_kb / KPS)
 };
+
+// Weight tile and token tile of work unit u. Weight tile fastest when x is
+// the larger operand: the pairs that run at the same time then share their x
+// tiles (each read once from DRAM, the other readers hit L2) and the smaller
+// weight stays in L2 across waves; token tile fastest otherwise.
+__device__ __forceinline__ void ts2_unit(const Ts2Params& p, int u, int& wt, int& tt) {
+  if (p.wt_fast) {
+    tt = u / p.num_w_tiles;
+    wt = u - tt * p.num_w_tiles;
+  } else {
+    wt = u / p.num_t_tiles;
+    tt = u - wt * p.num_t_tiles;
+  }
+}
 
 // tokens of pair tile tt given to the UMMA (N): all 256, or the remainder
 // rounded up to 32 (paired N is a multiple of 32; x rows past M read as zero)
@@ -170,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
   // the stream finishes. The producer waits for it before its x loads, the
   // epilogue before its stores.
 
-  const int num_units = p.num_w_tiles * p.num_t_tiles;  // token tile fastest
+  const int num_units = p.num_w_tiles * p.num_t_tiles;  // ordered by ts2_unit
   bool ok = true;
 
   if (warp == kWarpTma) {
@@ -191,14 +206,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
       for (int u = cid; u < num_units && pre < NS; u += ncl) {
         for (int st = 0; st < p.num_st && pre < NS; ++st, ++pre) {
           const int kb0 = st * KPS;
-          load_w(u / p.num_t_tiles, kb0, p.num_kb - kb0 < KPS ? p.num_kb - kb0 : KPS, pre);
+          int wt, tt;
+          ts2_unit(p, u, wt, tt);
+          load_w(wt, kb0, p.num_kb - kb0 < KPS ? p.num_kb - kb0 : KPS, pre);
         }
       }
       pdl_wait_prior_grids();
       int it = 0;
       for (int u = cid; u < num_units && ok; u += ncl) {
-        const int wt = u / p.num_t_tiles;
-        const int tt = u - wt * p.num_t_tiles;
+        int wt, tt;
+        ts2_unit(p, u, wt, tt);
         // this CTA's tokens: the second half of the UMMA's N starts at n_eff / 2
         const int tok0 = tt * BTP + (int)rank * (ts2_n_eff(p.M, tt) >> 1);
         for (int st = 0; st < p.num_st; ++st, ++it) {
@@ -234,7 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
     if (leader) {
       int it = 0, tcount = 0;
       for (int u = cid; u < num_units && ok; u += ncl, ++tcount) {
-        const int tt = u % p.num_t_tiles;
+        int wt, tt;
+        ts2_unit(p, u, wt, tt);
         const uint32_t idesc = umma_idesc_f16(BF16, 2 * BWC, ts2_n_eff(p.M, tt));
         ok = __all_sync(0xffffffffu, mbar_wait(empty_acc, (tcount & 1) ^ 1, p.status, 152, abort_flag));
         if (!ok) break;
@@ -275,7 +293,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
     auto load_sz = [&]() -> uint32_t {
       uint32_t v = 0;
       if (pu < num_units) {
-        const int n = (pu / p.num_t_tiles) * (2 * BWC) + (int)rank * BWC + row;
+        int pwt, ptt;
+        ts2_unit(p, pu, pwt, ptt);
+        const int n = pwt * (2 * BWC) + (int)rank * BWC + row;
         if (n < p.N) {
           const int64_t off = (int64_t)n * p.G + pg;
           v = (uint32_t)__ldg(sc16 + off) | ((uint32_t)__ldg(zr16 + off) << 16);
@@ -356,8 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts2_kernel(
     const int g = lane >> 2;  // fragment row: features g, g + 8 of each 16-lane half
     int tcount = 0;
     for (int u = cid; u < num_units && ok; u += ncl, ++tcount) {
-      const int wt = u / p.num_t_tiles;
-      const int tt = u - wt * p.num_t_tiles;
+      int wt, tt;
+      ts2_unit(p, u, wt, tt);
       ok = mbar_wait(full_acc, tcount & 1, p.status, 157, abort_flag);
       if (!named_bar_all(1, kEpiWarps * 32, ok)) {  // leave together if anyone gave up
         ok = false;
@@ -542,6 +562,10 @@ int run_prefill_ts2_linear(const LinearArgs& a, cudaStream_t stream) {
   p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
   p.num_w_tiles = (a.N + 2 * BWC - 1) / (2 * BWC);
   p.num_t_tiles = (a.M + BTP - 1) / BTP;
+  // x larger than the packed weight (e.g. down at M = 8192: 80 MB of x for
+  // 4.4 MB of weight): weight tile fastest
+  const int64_t w_bytes = (int64_t)a.N * (a.fmt == 0 ? a.K / 2 : a.K);
+  p.wt_fast = (int64_t)a.M * a.K * 2 > w_bytes ? 1 : 0;
   p.num_kb = (a.K + BK - 1) / BK;
   p.num_st = num_st;
   const int units = p.num_w_tiles * p.num_t_tiles;
