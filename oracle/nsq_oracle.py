@@ -189,6 +189,71 @@ def awq_quantize(weight: np.ndarray, group_size: int = 128):
 
 
 # ---------------------------------------------------------------------------
+# AutoAWQ checkpoint layout -> the reference layout
+# ---------------------------------------------------------------------------
+#
+# The reference's docstring (quantization.py:7) names AutoAWQ checkpoints, but
+# it ships no loader. AutoAWQ's GEMM format (the published WQLinear_GEMM
+# packing, restated here) stores, for in_features K, out_features N, groups G:
+#   qweight int32 [K, N/8]: the eight int4 values of output columns 8c..8c+7
+#           of input row k; nibble i (bits 4i..4i+3) holds column
+#           8c + AUTOAWQ_ORDER[i]
+#   qzeros  int32 [G, N/8]: the zero points of group g, packed the same way
+#   scales  fp16  [G, N]
+# and dequantises w[n, k] = (q[k, n] - z[g, n]) * s[g, n] with g = k // group.
+# The reference layout holds the same numbers as qweight [N, K/8] (nibble i of
+# word j = input column 8j+i), zeros fp16 [N, G] and scales fp16 [N, G].
+
+AUTOAWQ_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
+
+
+def autoawq_pack(q_kn: np.ndarray, z_gn: np.ndarray) -> tuple:
+    """int values q [K, N] and z [G, N] (0..15) -> AutoAWQ qweight [K, N/8], qzeros [G, N/8]."""
+    def pack(v):
+        v = np.asarray(v).astype(np.int64)
+        rows, n = v.shape
+        out = np.zeros((rows, n // 8), dtype=np.int64)
+        for i, col in enumerate(AUTOAWQ_ORDER):
+            out |= (v[:, col::8] & 0xF) << (4 * i)
+        return out.astype(np.uint32).view(np.int32)
+    return pack(q_kn), pack(z_gn)
+
+
+def autoawq_unpack(packed: np.ndarray) -> np.ndarray:
+    """AutoAWQ-packed int32 [R, N/8] -> uint8 [R, N]."""
+    p = np.asarray(packed).astype(np.int64) & 0xFFFFFFFF
+    rows, n8 = p.shape
+    out = np.empty((rows, n8 * 8), dtype=np.uint8)
+    for i, col in enumerate(AUTOAWQ_ORDER):
+        out[:, col::8] = ((p >> (4 * i)) & 0xF).astype(np.uint8)
+    return out
+
+
+def autoawq_to_reference(qweight, qzeros, scales):
+    """AutoAWQ (qweight [K, N/8], qzeros [G, N/8], scales [G, N]) -> the
+    reference's (qweight int32 [N, K/8], scales fp16 [N, G], zeros fp16 [N, G])."""
+    q = autoawq_unpack(qweight).T  # [N, K]
+    n, k = q.shape
+    packed = np.zeros((n, k // 8), dtype=np.int64)
+    for i in range(8):
+        packed |= q[:, i::8].astype(np.int64) << (4 * i)
+    z = autoawq_unpack(qzeros).T.astype(np.float16)  # [N, G]
+    s = np.ascontiguousarray(np.asarray(scales, dtype=np.float16).T)
+    return packed.astype(np.uint32).view(np.int32), s, np.ascontiguousarray(z)
+
+
+def autoawq_dequant(qweight, qzeros, scales, group_size: int) -> np.ndarray:
+    """fp16 [N, K] of an AutoAWQ layer with the reference's arithmetic
+    (quantization.py:139-148: fp16 (q - z) * s)."""
+    q = autoawq_unpack(qweight).T.astype(np.float16)
+    z = autoawq_unpack(qzeros).T.astype(np.float16)
+    s = np.asarray(scales, dtype=np.float16).T
+    n, k = q.shape
+    g = np.arange(k) // group_size
+    return (q - z[:, g]) * s[:, g]
+
+
+# ---------------------------------------------------------------------------
 # FP8 E4M3 (quantization.py:24-75)
 # ---------------------------------------------------------------------------
 
