@@ -584,6 +584,7 @@ def bench_config2_tok_s(torch, dist, device, rank, world, args):
     model = H.build_model(cfg, device=device, dtype=torch.bfloat16)
     H.quantize_projections_awq(model)
     H.init_awq(model, 2)
+    H.fuse_projections(model)  # q/k/v and gate/up+SiLU as one launch each at decode batch sizes
     prompts, outs = E.make_workload(32, 100, 512, 64, 128, cfg.vocab_size, seed=0)
     mine = list(range(rank, len(prompts), world))
     ps, os_ = [prompts[i] for i in mine], [outs[i] for i in mine]
@@ -611,8 +612,8 @@ def bench_config2_tok_s(torch, dist, device, rank, world, args):
             "unit": "output tokens/s (wall clock)", "elapsed_s": round(el, 4), "output_tokens": total_out,
             "prompt_tokens": sum(len(p) for p in prompts), "replicas": world,
             "decode_step_ms": round(step_ms, 4), "decode_step_batch": len(ps),
-            "method": "packed prefill + one CUDA-graph replay per decode step (harness engine); "
-                      "median of 3 runs after one warm-up"}
+            "method": "packed prefill + one CUDA-graph replay per decode step (harness engine), fused q/k/v and "
+                      "gate/up+SiLU launches at decode batch sizes; median of 3 runs after one warm-up"}
 
 
 def bench_config3_tok_s(torch, dist, device, rank, world, args):
@@ -633,6 +634,7 @@ def bench_config3_tok_s(torch, dist, device, rank, world, args):
     H.init_awq(model, 3)
     if world > 1:
         TP.tensor_parallel_model(model, world, rank)
+    H.fuse_projections(model)  # fused launches apply to M <= 32 only; 64 streams keep the separate layers
     eng = E.DecodeEngine(model, max_slots=streams, max_len=ctx + steps + 8, max_steps=steps + 4)
     g = torch.Generator(device=device).manual_seed(4 + rank)
     for kc, vc in eng.caches:

@@ -156,9 +156,10 @@ class Attention(nn.Module):
         slots are this batch, mask (bs, 1, 1, max_len) additive."""
         bs = hidden_states.shape[0]
         nh, nkv = self.num_heads, self.num_kv_heads
-        q = self.q_proj(hidden_states).view(bs, nh, self.head_dim)
-        k = self.k_proj(hidden_states).view(bs, nkv, self.head_dim)
-        v = self.v_proj(hidden_states).view(bs, nkv, self.head_dim)
+        q, k, v = self._qkv(hidden_states)
+        q = q.reshape(bs, nh, self.head_dim)
+        k = k.reshape(bs, nkv, self.head_dim)
+        v = v.reshape(bs, nkv, self.head_dim)
         q = apply_rope(q, cos, sin, positions)
         k = apply_rope(k, cos, sin, positions)
         rows = torch.arange(bs, device=hidden_states.device)
@@ -171,6 +172,12 @@ class Attention(nn.Module):
         out = F.scaled_dot_product_attention(qg, k_cache[:bs], v_cache[:bs], attn_mask=mask,
                                              scale=1.0 / math.sqrt(self.head_dim))
         return self.o_proj(out.reshape(bs, nh * self.head_dim))
+
+    def _qkv(self, h):
+        fused = getattr(self, "qkv", None)  # set by fuse_projections
+        if fused is not None:
+            return fused(h)
+        return self.q_proj(h), self.k_proj(h), self.v_proj(h)
 
     def forward_prefill(self, hidden_states, cos, sin, positions, k_cache, v_cache, slot):
         """One request's prompt (seq, hidden) into cache slot ``slot`` (causal)."""
@@ -199,6 +206,9 @@ class MLP(nn.Module):
         self.down_proj = nn.Linear(config.intermediate_size, config.hidden_size, bias=False)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        fused = getattr(self, "gate_up", None)  # set by fuse_projections
+        if fused is not None:
+            return self.down_proj(fused(x))
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
@@ -269,6 +279,20 @@ class CausalLM(nn.Module):
         for layer, (kc, vc) in zip(self.layers, caches):
             h = layer.forward_prefill(h, self.rope_cos, self.rope_sin, positions, kc, vc, slot)
         return self.lm_head(self.norm(h[-1:]))[0]
+
+
+def fuse_projections(model: CausalLM) -> CausalLM:
+    """Run q/k/v as one launch and gate/up with SiLU * up as one launch for
+    decode batches (nanosglang_b200.quantization.FusedProjections /
+    GateUpSiLU); larger batches keep the separate layers. Call after any
+    tensor-parallel sharding. The reference-shaped ``forward`` is unchanged."""
+    from nanosglang_b200.quantization import FusedProjections, GateUpSiLU
+    for layer in model.layers:
+        a, m = layer.self_attn, layer.mlp
+        a.qkv = FusedProjections(a.q_proj, a.k_proj, a.v_proj)
+        if hasattr(m, "gate_proj"):
+            m.gate_up = GateUpSiLU(m.gate_proj, m.up_proj)
+    return model
 
 
 def causal_mask(seq: int, dtype, device) -> torch.Tensor:

@@ -103,6 +103,40 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
                     int out_dtype, int64_t N, int64_t K, void* stream);
 
 /*
+ * Fused projections for decode batches (M <= 32): one launch over nw = 1..3
+ * weights of one format that read the same x, e.g. q/k/v, whose reference
+ * call sites are three separate linears (nano_sglang/model/causal_lm.py:
+ * 295-297). Weight i (its own buffers in the reference layout, ns[i] output
+ * rows, optional bias biases[i]) writes y columns [n_0 + .. + n_{i-1}, + n_i)
+ * of y [M, ldy]; the result equals the separate AWQLinear / FP8Linear
+ * forwards. Streams every weight row once (row-streaming kernel).
+ * M > 32 returns NSQ_ENOTSUP: call the single linears.
+ */
+int nsq_awq_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int nw, const int32_t* const* qweights,
+                         const uint16_t* const* scales, const uint16_t* const* zeros, const int64_t* ns,
+                         int64_t group_size, const void* const* biases, int bias_dtype, void* y, int64_t ldy,
+                         void* stream);
+int nsq_fp8_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int nw, const uint8_t* const* weights,
+                         const float* const* weight_scales, const int64_t* ns, const void* const* biases,
+                         int bias_dtype, void* y, int64_t ldy, void* stream);
+
+/*
+ * Fused gate/up projection with the SwiGLU activation for decode batches
+ * (M <= 32): y [M, N] = SiLU(x gate^T) * (x up^T) in one launch, the inner
+ * expression of MLP.forward (nano_sglang/model/causal_lm.py:482) computed in
+ * fp32 and rounded once. gate and up are two separate weights [N, K] in the
+ * reference layout (no concatenated copy). M > 32 returns NSQ_ENOTSUP.
+ */
+int nsq_awq_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N, const int32_t* qweight_gate,
+                         const uint16_t* scales_gate, const uint16_t* zeros_gate, const int32_t* qweight_up,
+                         const uint16_t* scales_up, const uint16_t* zeros_up, int64_t group_size, void* y,
+                         void* stream);
+int nsq_fp8_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N, const uint8_t* weight_gate,
+                         const float* scale_gate, const uint8_t* weight_up, const float* scale_up, void* y,
+                         void* stream);
+
+/*
+ * AWQ quantiser, bit-exact with AWQLinear.from_linear/*
  * AWQ quantiser, bit-exact with AWQLinear.from_linear
  * (quantization.py:154-194): per (row, group) asymmetric min/max int4,
  * sequential nibble packing, columns past 8*(K/8) dropped. w is row-major
@@ -111,6 +145,21 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
  */
 int nsq_awq_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int64_t group_size,
                      int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream);
+
+/*
+ * AutoAWQ checkpoint layer -> the reference layout, bit-exact repack (no
+ * arithmetic on the values). The reference's module docstring names AutoAWQ
+ * checkpoints (quantization.py:7) but ships no loader; this is that loader's
+ * device step. Input, AutoAWQ's GEMM format for in_features K, out_features N,
+ * G = K / group_size: qweight_kn8 int32 [K, N/8] and qzeros_gn8 int32
+ * [G, N/8], eight int4 values per word along N with nibble i holding column
+ * 8c + {0,2,4,6,1,3,5,7}[i]; scales_gn fp16 [G, N]. Output, the AWQLinear
+ * buffers (quantization.py:107-119): qweight int32 [N, K/8], scales and
+ * zeros fp16 [N, G]. Requires K % 8 == 0, N % 8 == 0, K % group_size == 0.
+ */
+int nsq_awq_from_autoawq(const int32_t* qweight_kn8, const int32_t* qzeros_gn8, const uint16_t* scales_gn,
+                         int64_t K, int64_t N, int64_t group_size, int32_t* qweight, uint16_t* scales,
+                         uint16_t* zeros, void* stream);
 
 /* Bytes of device workspace nsq_fp8_quantize needs (absmax reduction). */
 size_t nsq_fp8_quantize_workspace_size(int64_t N, int64_t K);

@@ -44,9 +44,19 @@ SIGNATURES = {
                                c_int64, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "nsq_fp8_linear": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                                c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "nsq_awq_linear_multi": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_int64, c_void_p, c_int, c_void_p, c_int64, c_void_p]),
+    "nsq_fp8_linear_multi": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_int, c_void_p, c_int64, c_void_p]),
+    "nsq_awq_gate_up_silu": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "nsq_fp8_gate_up_silu": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_void_p]),
     "nsq_fp8_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "nsq_awq_quantize": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                                  c_void_p]),
+    "nsq_awq_from_autoawq": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                                     c_void_p, c_void_p]),
     "nsq_fp8_quantize_workspace_size": (c_size_t, [c_int64, c_int64]),
     "nsq_fp8_quantize": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_size_t,
                                  c_void_p]),

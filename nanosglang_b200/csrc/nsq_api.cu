@@ -306,6 +306,96 @@ int nsq_fp8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
   return linear_common(a, static_cast<cudaStream_t>(stream));
 }
 
+// Fused projections over weights that share x (M <= 32, the decode batches):
+// mode 0 writes weight i's outputs to y columns [sum n_<i, + n_i); mode 1
+// takes (gate, up) and writes SiLU(x gate^T) * (x up^T).
+static int fused_common(int fmt, int mode, const void* x, int x_dtype, int64_t M, int64_t K, int nw,
+                        const void* const* w, const uint16_t* const* scales, const uint16_t* const* zeros,
+                        const float* const* wscales, const int64_t* ns, int64_t group_size,
+                        const void* const* biases, int bias_dtype, void* y, int64_t ldy, void* stream) {
+  if (nw < 1 || nw > 3 || (mode == 1 && nw != 2)) return NSQ_EINVAL;
+  if (M < 0 || K <= 0 || M > kIntMax || K > kIntMax || ldy <= 0 || ldy > kIntMax) return NSQ_EINVAL;
+  if (!valid_act_dtype(x_dtype) || !valid_bias_dtype(bias_dtype)) return NSQ_EINVAL;
+  if (!w || !ns || (fmt == 0 && (!scales || !zeros)) || (fmt == 1 && !wscales)) return NSQ_EINVAL;
+  if ((bias_dtype == NSQ_DTYPE_NONE) != (biases == nullptr)) return NSQ_EINVAL;
+  if (fmt == 0 && (group_size <= 0 || group_size % 128 != 0)) return NSQ_ENOTSUP;
+  if (K % (fmt == 0 ? 32 : 16) != 0) return NSQ_ENOTSUP;  // 16-byte row pitch of the weights for TMA
+  if (M > 32) return NSQ_ENOTSUP;                         // decode batches only: call the single linears
+  int64_t cols = 0;
+  for (int i = 0; i < nw; ++i) {
+    if (ns[i] <= 0 || ns[i] > kIntMax || !w[i]) return NSQ_EINVAL;
+    if (!aligned16(w[i])) return NSQ_EALIGN;
+    if (fmt == 0 && (!scales[i] || !zeros[i])) return NSQ_EINVAL;
+    if (fmt == 1 && !wscales[i]) return NSQ_EINVAL;
+    if (mode == 1 && ns[i] != ns[0]) return NSQ_EINVAL;
+    cols += mode == 0 ? ns[i] : 0;
+  }
+  if (mode == 1) cols = ns[0];
+  if (cols > ldy) return NSQ_EINVAL;
+  if (M == 0) return NSQ_OK;
+  if (!x || !y) return NSQ_EINVAL;
+  if (!aligned16(x) || !aligned16(y)) return NSQ_EALIGN;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  RowsLaunch L{};
+  L.fmt = fmt;
+  L.x = x;
+  L.x_bf16 = x_dtype == NSQ_DTYPE_BF16;
+  L.M = (int)M;
+  L.K = (int)K;
+  L.y = y;
+  L.ldy = (int)ldy;
+  L.group_size = fmt == 0 ? (int)group_size : 0;
+  L.bias_dtype = bias_dtype;
+  L.mode = mode;
+  L.nw = nw;
+  int64_t col = 0;
+  for (int i = 0; i < nw; ++i) {
+    L.w[i] = RowsWeight{w[i], fmt == 0 ? scales[i] : nullptr, fmt == 0 ? zeros[i] : nullptr,
+                        fmt == 1 ? wscales[i] : nullptr, biases ? biases[i] : nullptr, (int)ns[i],
+                        mode == 0 ? (int)col : 0};
+    col += ns[i];
+  }
+  return run_decode_rows(L, static_cast<cudaStream_t>(stream));
+}
+
+int nsq_awq_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int nw, const int32_t* const* qweights,
+                         const uint16_t* const* scales, const uint16_t* const* zeros, const int64_t* ns,
+                         int64_t group_size, const void* const* biases, int bias_dtype, void* y, int64_t ldy,
+                         void* stream) {
+  return fused_common(0, 0, x, x_dtype, M, K, nw, reinterpret_cast<const void* const*>(qweights), scales, zeros,
+                      nullptr, ns, group_size, biases, bias_dtype, y, ldy, stream);
+}
+
+int nsq_fp8_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int nw, const uint8_t* const* weights,
+                         const float* const* weight_scales, const int64_t* ns, const void* const* biases,
+                         int bias_dtype, void* y, int64_t ldy, void* stream) {
+  return fused_common(1, 0, x, x_dtype, M, K, nw, reinterpret_cast<const void* const*>(weights), nullptr, nullptr,
+                      weight_scales, ns, 0, biases, bias_dtype, y, ldy, stream);
+}
+
+int nsq_awq_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N, const int32_t* qweight_gate,
+                         const uint16_t* scales_gate, const uint16_t* zeros_gate, const int32_t* qweight_up,
+                         const uint16_t* scales_up, const uint16_t* zeros_up, int64_t group_size, void* y,
+                         void* stream) {
+  const int32_t* qw[2] = {qweight_gate, qweight_up};
+  const uint16_t* sc[2] = {scales_gate, scales_up};
+  const uint16_t* zr[2] = {zeros_gate, zeros_up};
+  const int64_t ns[2] = {N, N};
+  return fused_common(0, 1, x, x_dtype, M, K, 2, reinterpret_cast<const void* const*>(qw), sc, zr, nullptr, ns,
+                      group_size, nullptr, NSQ_DTYPE_NONE, y, N, stream);
+}
+
+int nsq_fp8_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N, const uint8_t* weight_gate,
+                         const float* scale_gate, const uint8_t* weight_up, const float* scale_up, void* y,
+                         void* stream) {
+  const uint8_t* wt[2] = {weight_gate, weight_up};
+  const float* ws[2] = {scale_gate, scale_up};
+  const int64_t ns[2] = {N, N};
+  return fused_common(1, 1, x, x_dtype, M, K, 2, reinterpret_cast<const void* const*>(wt), nullptr, nullptr, ws, ns,
+                      0, nullptr, NSQ_DTYPE_NONE, y, N, stream);
+}
+
 int nsq_awq_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int64_t group_size,
                      int32_t* qweight, uint16_t* scales, uint16_t* zeros, void* stream) {
   if (N < 0 || K < 8 || group_size <= 0) return NSQ_EINVAL;
@@ -318,6 +408,19 @@ int nsq_awq_quantize(const void* w, int w_dtype, int64_t N, int64_t K, int64_t g
   if (rc != NSQ_OK) return rc;
   cudaError_t e = launch_awq_quantize(w, w_dtype, N, K, group_size, qweight, scales, zeros,
                                       static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+int nsq_awq_from_autoawq(const int32_t* qweight_kn8, const int32_t* qzeros_gn8, const uint16_t* scales_gn,
+                         int64_t K, int64_t N, int64_t group_size, int32_t* qweight, uint16_t* scales,
+                         uint16_t* zeros, void* stream) {
+  if (K <= 0 || N <= 0 || group_size <= 0 || K % 8 != 0 || N % 8 != 0 || K % group_size != 0) return NSQ_EINVAL;
+  if (K > kIntMax || N > kIntMax) return NSQ_EINVAL;
+  if (!qweight_kn8 || !qzeros_gn8 || !scales_gn || !qweight || !scales || !zeros) return NSQ_EINVAL;
+  int rc = check_device();
+  if (rc != NSQ_OK) return rc;
+  cudaError_t e = launch_awq_from_autoawq(qweight_kn8, qzeros_gn8, scales_gn, K, N, group_size, qweight, scales,
+                                          zeros, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
 }
 

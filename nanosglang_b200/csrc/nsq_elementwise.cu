@@ -5,6 +5,8 @@
 //     (quantization.py:51)
 //   * AWQ / FP8 quantisers, bit-exact with AWQLinear.from_linear
 //     (quantization.py:154-194) and FP8Linear.from_linear (quantization.py:54-75)
+//   * repack of an AutoAWQ (GEMM-format) layer into the reference layout, the
+//     loader the reference's docstring names (quantization.py:7) but lacks
 //
 // All are grid-stride kernels sized to a multiple of the SM count; each thread
 // moves 16-byte vectors where the layout allows.
@@ -202,6 +204,50 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(const void* __restric
 }
 
 // ---------------------------------------------------------------------------
+// AutoAWQ GEMM format -> reference layout. AutoAWQ packs eight output columns
+// per int32 word along N with nibble i holding column 8c + order[i], order =
+// {0, 2, 4, 6, 1, 3, 5, 7}; the reference packs eight input columns per word
+// along K, nibble i = column 8j + i. Column n sits in nibble kAutoAwqNibble[n % 8].
+__constant__ int kAutoAwqNibble[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+
+// One thread per output word (n, j), j fastest so the stores are coalesced;
+// it gathers nibble kAutoAwqNibble[n % 8] of input rows 8j .. 8j+7.
+__global__ void __launch_bounds__(256) awq_from_autoawq_qweight_kernel(const uint32_t* __restrict__ qw_kn,
+                                                                       uint32_t* __restrict__ out, int64_t N,
+                                                                       int64_t K) {
+  const int64_t k8 = K / 8, n8 = N / 8;
+  const int64_t total = N * k8;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = idx / k8;
+    const int64_t j = idx - n * k8;
+    const int sh = 4 * kAutoAwqNibble[n & 7];
+    const uint32_t* src = qw_kn + (j * 8) * n8 + (n >> 3);
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= ((__ldg(src + i * n8) >> sh) & 0xFu) << (4 * i);
+    out[idx] = w;
+  }
+}
+
+// One thread per (n, g), g fastest: zero point (int4 -> fp16, exact) and scale
+// transposed from [G, N] to [N, G].
+__global__ void __launch_bounds__(256) awq_from_autoawq_sz_kernel(const uint32_t* __restrict__ qz_gn,
+                                                                  const __half* __restrict__ s_gn,
+                                                                  __half* __restrict__ s_out,
+                                                                  __half* __restrict__ z_out, int64_t N,
+                                                                  int64_t G) {
+  const int64_t total = N * G;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = idx / G;
+    const int64_t g = idx - n * G;
+    const uint32_t w = __ldg(qz_gn + g * (N / 8) + (n >> 3));
+    z_out[idx] = __uint2half_rn((w >> (4 * kAutoAwqNibble[n & 7])) & 0xFu);
+    s_out[idx] = s_gn[g * N + n];
+  }
+}
+
 // Host launchers (validated by nsq_api.cu before they are called)
 // ---------------------------------------------------------------------------
 static int grid_for(int64_t items, int threads) {
@@ -247,6 +293,24 @@ cudaError_t launch_awq_quantize(const void* w, int dtype, int64_t N, int64_t K, 
   awq_quantize_kernel<<<grid_for(N * G * 32, 256), 256, 0, stream>>>(
       w, dtype, N, K, gs, G, reinterpret_cast<uint32_t*>(qweight),
       reinterpret_cast<__half*>(scales), reinterpret_cast<__half*>(zeros), use_atomic);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_awq_from_autoawq(const int32_t* qweight_kn8, const int32_t* qzeros_gn8,
+                                    const uint16_t* scales_gn, int64_t K, int64_t N, int64_t gs,
+                                    int32_t* qweight, uint16_t* scales, uint16_t* zeros, cudaStream_t stream) {
+  const int64_t G = K / gs;
+  if (N * (K / 8) > 0) {
+    awq_from_autoawq_qweight_kernel<<<grid_for(N * (K / 8), 256), 256, 0, stream>>>(
+        reinterpret_cast<const uint32_t*>(qweight_kn8), reinterpret_cast<uint32_t*>(qweight), N, K);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (N * G > 0) {
+    awq_from_autoawq_sz_kernel<<<grid_for(N * G, 256), 256, 0, stream>>>(
+        reinterpret_cast<const uint32_t*>(qzeros_gn8), reinterpret_cast<const __half*>(scales_gn),
+        reinterpret_cast<__half*>(scales), reinterpret_cast<__half*>(zeros), N, G);
+  }
   return cudaGetLastError();
 }
 

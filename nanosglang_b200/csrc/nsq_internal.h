@@ -31,6 +31,9 @@ cudaError_t launch_fp8_dequant(const uint8_t* w, const float* scale, void* out, 
 cudaError_t launch_awq_quantize(const void* w, int dtype, int64_t N, int64_t K, int64_t gs,
                                 int32_t* qweight, uint16_t* scales, uint16_t* zeros,
                                 cudaStream_t stream);
+cudaError_t launch_awq_from_autoawq(const int32_t* qweight_kn8, const int32_t* qzeros_gn8,
+                                    const uint16_t* scales_gn, int64_t K, int64_t N, int64_t gs,
+                                    int32_t* qweight, uint16_t* scales, uint16_t* zeros, cudaStream_t stream);
 cudaError_t launch_fp8_quantize(const void* w, int dtype, int64_t total, uint8_t* codes,
                                 float* scale, void* workspace, cudaStream_t stream);
 
@@ -53,6 +56,33 @@ int run_decode_wave_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 6
 int run_decode_stream_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 64, persistent weight ring
 int run_decode_linear(const LinearArgs& a, cudaStream_t stream);   // M <= 64, one or more waves
 int decode_linear_ctas(const LinearArgs& a);  // CTAs run_decode_linear launches, -1 if it cannot
+// Row-streaming decode kernel over 1..3 weights sharing x (M <= 32). mode 0:
+// weight i writes y columns [ycol, ycol + n); mode 1: w[0] = gate, w[1] =
+// up (same n), y[:, :n] = SiLU(x gate^T) * (x up^T).
+struct RowsWeight {
+  const void* w;           // qweight [n, K/8] (AWQ) or weight_fp8 [n, K] (FP8)
+  const uint16_t* scales;  // AWQ
+  const uint16_t* zeros;   // AWQ
+  const float* wscale;     // FP8
+  const void* bias;        // [n] or null (dtype: RowsLaunch::bias_dtype)
+  int n;
+  int ycol;
+};
+struct RowsLaunch {
+  int fmt;
+  const void* x;
+  int x_bf16;
+  int M, K;
+  void* y;
+  int ldy;  // row stride of y (elements)
+  int group_size;
+  int bias_dtype;
+  int mode;
+  int nw;
+  RowsWeight w[3];
+};
+int run_decode_rows(const RowsLaunch& L, cudaStream_t stream);
+int run_decode_rows_linear(const LinearArgs& a, cudaStream_t stream);
 // prefill: the weight tile dequantised into tensor memory (A operand), tokens
 // as UMMA N. One CTA per 128 weight rows x 64/128 tokens, K optionally split
 // over a cluster (small outputs, few-tile long-K layers), or CTA pairs with

@@ -125,6 +125,32 @@ def awq_quantize(weight: torch.Tensor, group_size: int = 128):
     return qweight, scales, zeros
 
 
+def awq_from_autoawq(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, group_size: int):
+    """Repack one AutoAWQ (GEMM-format) layer into the reference layout, bit-exact.
+
+    qweight int32 [K, N/8], qzeros int32 [K/group_size, N/8], scales fp16
+    [K/group_size, N] -> (qweight int32 [N, K/8], scales fp16 [N, G], zeros
+    fp16 [N, G]), the AWQLinear buffers of quantization.py:107-119.
+    """
+    _require_cuda(qweight, qzeros, scales, what="awq_from_autoawq")
+    if qweight.dtype != torch.int32 or qzeros.dtype != torch.int32 or scales.dtype != torch.float16:
+        raise TypeError("AutoAWQ layers hold int32 qweight/qzeros and float16 scales")
+    k, n8 = qweight.shape
+    n = n8 * 8
+    g = k // group_size
+    if qzeros.shape != (g, n8) or scales.shape != (g, n):
+        raise ValueError(f"AutoAWQ shapes disagree: qweight {tuple(qweight.shape)}, qzeros {tuple(qzeros.shape)}, "
+                         f"scales {tuple(scales.shape)}, group_size {group_size}")
+    qweight, qzeros, scales = qweight.contiguous(), qzeros.contiguous(), scales.contiguous()
+    out_q = torch.empty(n, k // 8, dtype=torch.int32, device=qweight.device)
+    out_s = torch.empty(n, g, dtype=torch.float16, device=qweight.device)
+    out_z = torch.empty(n, g, dtype=torch.float16, device=qweight.device)
+    rc = _lib.load().nsq_awq_from_autoawq(_ptr(qweight), _ptr(qzeros), _ptr(scales), k, n, group_size, _ptr(out_q),
+                                          _ptr(out_s), _ptr(out_z), _stream(qweight))
+    _lib.check(rc, "nsq_awq_from_autoawq")
+    return out_q, out_s, out_z
+
+
 # ---------------------------------------------------------------------------
 # FP8
 # ---------------------------------------------------------------------------
@@ -203,3 +229,120 @@ def fp8_quantize(weight: torch.Tensor):
     _lib.check(rc, "nsq_fp8_quantize")
     absmax_zero = ws[:4].view(torch.int32)[0] == 0
     return codes.view(torch.float8_e4m3fn), scale, absmax_zero
+
+
+# ---------------------------------------------------------------------------
+# Fused projections for decode batches (row-streaming kernel, M <= 32)
+# ---------------------------------------------------------------------------
+
+FUSED_MAX_M = 32
+
+
+def _unwrap(mod):
+    """The quantized module behind a tensor-parallel wrapper (its local shard)."""
+    return getattr(mod, "linear", mod)
+
+
+def _ptr_array(vals, ctype=None):
+    import ctypes
+    arr = (ctypes.c_void_p * len(vals))(*vals) if ctype is None else (ctype * len(vals))(*vals)
+    return arr
+
+
+def linear_multi(x: torch.Tensor, mods) -> Optional[list]:
+    """One launch for 1..3 AWQLinear (or 1..3 FP8Linear) layers that read the
+    same x, e.g. q/k/v. Returns their outputs as views of one [M, sum N]
+    buffer, or None when the fused kernel does not apply (M > 32, mixed
+    formats, bias dtypes that differ, group sizes that differ)."""
+    import ctypes
+    mods = [_unwrap(m) for m in mods]
+    kinds = {type(m).__name__ for m in mods}
+    if len(kinds) != 1 or x.dtype not in _ACT_CODES:
+        return None
+    k = x.shape[-1]
+    lead = x.shape[:-1]
+    x2 = _aligned(x.reshape(-1, k))
+    m = x2.shape[0]
+    if m == 0 or m > FUSED_MAX_M:
+        return None
+    biases = [mm.bias for mm in mods]
+    has_bias = [b is not None for b in biases]
+    if any(has_bias) and not all(has_bias):
+        biases = [b if b is not None else torch.zeros(mm.out_features, device=x.device, dtype=x.dtype)
+                  for b, mm in zip(biases, mods)]
+    bias_dtypes = {b.dtype for b in biases if b is not None}
+    if len(bias_dtypes) > 1:
+        return None
+    biases = [b.contiguous() for b in biases] if any(has_bias) else None
+    bcode = _BIAS_CODES[biases[0].dtype] if biases else _lib.DTYPE_NONE
+    ns = [mm.out_features for mm in mods]
+    y = torch.empty(m, sum(ns), dtype=x.dtype, device=x.device)
+    n_arr = (ctypes.c_int64 * len(ns))(*ns)
+    b_arr = _ptr_array([b.data_ptr() for b in biases]) if biases else None
+    lib = _lib.load()
+    if kinds == {"AWQLinear"}:
+        gs = {mm.group_size for mm in mods}
+        if len(gs) != 1 or any(mm.in_features != k for mm in mods):
+            return None
+        qws = [_aligned(mm.qweight) for mm in mods]
+        scs = [mm.scales.contiguous() for mm in mods]
+        zrs = [mm.zeros.contiguous() for mm in mods]
+        rc = lib.nsq_awq_linear_multi(_ptr(x2), _ACT_CODES[x.dtype], m, k, len(mods),
+                                      _ptr_array([t.data_ptr() for t in qws]), _ptr_array([t.data_ptr() for t in scs]),
+                                      _ptr_array([t.data_ptr() for t in zrs]), n_arr, gs.pop(), b_arr, bcode, _ptr(y),
+                                      y.shape[1], _stream(x))
+    elif kinds == {"FP8Linear"}:
+        ws = [_aligned(_u8(mm.weight_fp8)) for mm in mods]
+        if any(w.shape[1] != k for w in ws):
+            return None
+        scs = [_scale_arg(mm.weight_scale) for mm in mods]
+        rc = lib.nsq_fp8_linear_multi(_ptr(x2), _ACT_CODES[x.dtype], m, k, len(mods),
+                                      _ptr_array([t.data_ptr() for t in ws]), _ptr_array([t.data_ptr() for t in scs]),
+                                      n_arr, b_arr, bcode, _ptr(y), y.shape[1], _stream(x))
+    else:
+        return None
+    if rc == _lib.ENOTSUP:
+        return None
+    _lib.check(rc, "nsq_*_linear_multi")
+    outs, c0 = [], 0
+    for n in ns:
+        outs.append(y[:, c0:c0 + n].reshape(*lead, n))
+        c0 += n
+    return outs
+
+
+def gate_up_silu(x: torch.Tensor, gate, up) -> Optional[torch.Tensor]:
+    """SiLU(gate(x)) * up(x) in one launch (MLP.forward's inner expression,
+    causal_lm.py:482) for AWQ or FP8 gate/up layers without bias; None when
+    the fused kernel does not apply (M > 32, bias, mismatched layers)."""
+    gate, up = _unwrap(gate), _unwrap(up)
+    if type(gate) is not type(up) or x.dtype not in _ACT_CODES or gate.bias is not None or up.bias is not None:
+        return None
+    k = x.shape[-1]
+    lead = x.shape[:-1]
+    x2 = _aligned(x.reshape(-1, k))
+    m = x2.shape[0]
+    n = gate.out_features
+    if m == 0 or m > FUSED_MAX_M or up.out_features != n:
+        return None
+    y = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    lib = _lib.load()
+    if type(gate).__name__ == "AWQLinear":
+        if gate.group_size != up.group_size or gate.in_features != k or up.in_features != k:
+            return None
+        rc = lib.nsq_awq_gate_up_silu(_ptr(x2), _ACT_CODES[x.dtype], m, k, n, _ptr(_aligned(gate.qweight)),
+                                      _ptr(gate.scales.contiguous()), _ptr(gate.zeros.contiguous()),
+                                      _ptr(_aligned(up.qweight)), _ptr(up.scales.contiguous()),
+                                      _ptr(up.zeros.contiguous()), gate.group_size, _ptr(y), _stream(x))
+    elif type(gate).__name__ == "FP8Linear":
+        wg, wu = _aligned(_u8(gate.weight_fp8)), _aligned(_u8(up.weight_fp8))
+        if wg.shape[1] != k or wu.shape[1] != k:
+            return None
+        rc = lib.nsq_fp8_gate_up_silu(_ptr(x2), _ACT_CODES[x.dtype], m, k, n, _ptr(wg), _ptr(_scale_arg(gate.weight_scale)),
+                                      _ptr(wu), _ptr(_scale_arg(up.weight_scale)), _ptr(y), _stream(x))
+    else:
+        return None
+    if rc == _lib.ENOTSUP:
+        return None
+    _lib.check(rc, "nsq_*_gate_up_silu")
+    return y.reshape(*lead, n)

@@ -32,7 +32,7 @@ import torch.nn as nn
 
 from . import ops
 
-__all__ = ["FP8Linear", "AWQLinear", "quantize_model"]
+__all__ = ["FP8Linear", "AWQLinear", "quantize_model", "load_autoawq_state_dict", "FusedProjections", "GateUpSiLU"]
 
 
 class FP8Linear(nn.Module):
@@ -126,6 +126,80 @@ class AWQLinear(nn.Module):
         if has_bias:
             awq.bias = nn.Parameter(linear.bias.data.clone())
         return awq
+
+
+class FusedProjections(nn.Module):
+    """Projections that read the same x (q/k/v), run as one launch for decode
+    batches (M <= 32) and as the separate layers otherwise.
+
+    The layers stay where they are (``attn.q_proj`` etc.): this module keeps
+    plain references, so the model's state_dict is unchanged. The reference
+    calls q/k/v one by one (causal_lm.py:295-297); ``forward`` returns the
+    same three tensors.
+    """
+
+    def __init__(self, *layers: nn.Module):
+        super().__init__()
+        self._layers = list(layers)  # not registered: no duplicate state
+
+    def forward(self, x: torch.Tensor):
+        outs = ops.linear_multi(x, self._layers)
+        if outs is None:
+            outs = [layer(x) for layer in self._layers]
+        return tuple(outs)
+
+
+class GateUpSiLU(nn.Module):
+    """``F.silu(gate_proj(x)) * up_proj(x)`` (causal_lm.py:482) as one launch
+    for decode batches (M <= 32; the activation is applied in fp32 and
+    rounded once), the separate layers otherwise. Keeps plain references to
+    the two layers (the state_dict is unchanged)."""
+
+    def __init__(self, gate_proj: nn.Module, up_proj: nn.Module):
+        super().__init__()
+        self._gate = [gate_proj]
+        self._up = [up_proj]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        y = ops.gate_up_silu(x, self._gate[0], self._up[0])
+        if y is None:
+            y = torch.nn.functional.silu(self._gate[0](x)) * self._up[0](x)
+        return y
+
+
+def load_autoawq_state_dict(model: nn.Module, state_dict: dict, group_size: int = 128) -> list:
+    """Load an AutoAWQ checkpoint (GEMM format) into a model whose projections
+    are AWQLinear modules (after ``quantize_model(model, "awq", group_size)``).
+
+    For every AWQLinear ``name``, the checkpoint's ``{prefix}{name}.qweight``
+    [K, N/8], ``.qzeros`` [K/G, N/8] and ``.scales`` [K/G, N] are repacked on
+    the module's device into the reference layout; ``.bias`` is copied when
+    present. ``prefix`` is found automatically among "", "model." (Hugging
+    Face checkpoints keep the decoder under ``model.``). Returns the names of
+    the modules that were loaded.
+    """
+    loaded = []
+    for name, mod in model.named_modules():
+        if not isinstance(mod, AWQLinear):
+            continue
+        for prefix in ("", "model."):
+            key = f"{prefix}{name}."
+            if key + "qweight" in state_dict:
+                break
+        else:
+            continue
+        dev = mod.qweight.device
+        qw, s, z = ops.awq_from_autoawq(state_dict[key + "qweight"].to(dev), state_dict[key + "qzeros"].to(dev),
+                                        state_dict[key + "scales"].to(dev), group_size)
+        if qw.shape != mod.qweight.shape or s.shape != mod.scales.shape:
+            raise ValueError(f"{name}: checkpoint shape {tuple(qw.shape)} does not fit {tuple(mod.qweight.shape)}")
+        mod.qweight.copy_(qw)
+        mod.scales.copy_(s)
+        mod.zeros.copy_(z)
+        if mod.bias is not None and key + "bias" in state_dict:
+            mod.bias.data.copy_(state_dict[key + "bias"].to(mod.bias.device, mod.bias.dtype))
+        loaded.append(name)
+    return loaded
 
 
 def _quantize_fp8(child: nn.Linear, group_size: int) -> nn.Module:

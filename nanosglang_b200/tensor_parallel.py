@@ -279,6 +279,9 @@ class TPMLP(nn.Module):
         return out
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        fused = getattr(self, "gate_up", None)  # a GateUpSiLU over this rank's gate/up shards, if installed
+        if fused is not None:
+            return self.down_proj(fused(x))
         return self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
 
 

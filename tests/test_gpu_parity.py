@@ -471,3 +471,49 @@ def test_fp8_linear_every_code(m, dtype):
                        torch.tensor(scale).cuda())
     ref = O.fp8_linear(_to_np(x), codes, scale)
     assert O.rel_fro(_to_np(y), ref) <= GEMM_TOL
+
+
+# ---------------------------------------------------------------------------
+# AutoAWQ checkpoint layout -> reference layout (the loader quantization.py:7 names)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("k,n,gs", [(896, 4864, 128), (4096, 1024, 128), (256, 72, 64), (128, 8, 32)])
+def test_awq_from_autoawq_bit_exact(k, n, gs):
+    from nanosglang_b200 import ops
+    rng = np.random.default_rng(k + n)
+    q = rng.integers(0, 16, (k, n))
+    z = rng.integers(0, 16, (k // gs, n))
+    s = (rng.random((k // gs, n)) * 0.009 + 0.001).astype(np.float16)
+    aq, az = O.autoawq_pack(q, z)
+    rq, rs, rz = O.autoawq_to_reference(aq, az, s)
+    tq, ts, tz = ops.awq_from_autoawq(torch.from_numpy(aq).cuda(), torch.from_numpy(az).cuda(),
+                                      torch.from_numpy(s).cuda(), gs)
+    assert np.array_equal(tq.cpu().numpy(), rq)
+    assert np.array_equal(ts.cpu().numpy().view(np.uint16), rs.view(np.uint16))
+    assert np.array_equal(tz.cpu().numpy().view(np.uint16), rz.view(np.uint16))
+    # the repacked layer dequantises to AutoAWQ's own weights, bit for bit
+    w = ops.awq_dequant(tq, ts, tz, k, gs)
+    assert np.array_equal(w.cpu().numpy().view(np.uint16), O.autoawq_dequant(aq, az, s, gs).view(np.uint16))
+
+
+def test_load_autoawq_state_dict_into_quantized_model():
+    from nanosglang_b200 import quantization as Q
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Linear(256, 512, bias=True), nn.Linear(512, 256, bias=False)).cuda()
+    Q.quantize_model(model, "awq", 128)
+    rng = np.random.default_rng(3)
+    sd, refs = {}, {}
+    for name, (k, n) in {"0": (256, 512), "1": (512, 256)}.items():
+        q, z = rng.integers(0, 16, (k, n)), rng.integers(0, 16, (k // 128, n))
+        s = (rng.random((k // 128, n)) * 0.009 + 0.001).astype(np.float16)
+        aq, az = O.autoawq_pack(q, z)
+        sd[f"model.{name}.qweight"], sd[f"model.{name}.qzeros"] = torch.from_numpy(aq), torch.from_numpy(az)
+        sd[f"model.{name}.scales"] = torch.from_numpy(s)
+        refs[name] = (aq, az, s, k)
+    sd["model.0.bias"] = torch.randn(512)
+    assert sorted(Q.load_autoawq_state_dict(model, sd, 128)) == ["0", "1"]
+    x = torch.randn(5, 256, device="cuda", dtype=torch.float16)
+    aq, az, s, k = refs["0"]
+    ref = _to_np(x) @ O.autoawq_dequant(aq, az, s, 128).astype(np.float32).T + sd["model.0.bias"].numpy()
+    assert O.rel_fro(_to_np(model[0](x)), ref) <= GEMM_TOL
