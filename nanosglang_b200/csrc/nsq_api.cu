@@ -221,6 +221,21 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
       const TsPlan tp = prefill_ts_plan(a.fmt, a.M, a.K, a.N);
       if (tp.tokens_per_tile > 0) return run_prefill_ts_linear(a, tp, stream);
     }
+    // Large weights at up to 32 tokens (FP8) or 17..32 tokens (AWQ): the
+    // row-streaming kernel (B200, CUDA-graph chains: FP8 4096 -> 14336 at
+    // M = 16 27.7 -> 20.7 us; AWQ at M = 32: 4096 -> 14336 45 -> 37 us,
+    // 14336 -> 4096 90 -> 49 us, 4096 -> 4096 26 -> 17 us; AWQ at M <= 16
+    // and the Qwen2.5-0.5B shapes stay on the kernels below). AWQ group sizes
+    // 32 and 64 run here for every M <= 32.
+    const bool small_group = a.fmt == 0 && a.group_size % 128 != 0;
+    if (a.M <= 32 && (small_group || ((int64_t)a.K * a.N >= ((int64_t)1 << 24) && (a.fmt == 1 || a.M > 16)))) {
+      const int rc = run_decode_rows_linear(a, stream);
+      if (rc != NSQ_ENOTSUP || small_group) return rc;
+    }
+    if (small_group) {  // 33..64 tokens: the one-CTA tcgen05 kernel handles groups of 32 and 64
+      const TsPlan tp = prefill_ts_plan(a.fmt, a.M, a.K, a.N);
+      return run_prefill_ts_linear(a, tp.tokens_per_tile > 0 ? tp : TsPlan{64, 1}, stream);
+    }
     const int ctas = decode_linear_ctas(a);
     if (ctas < 0 || ctas > 2 * num_sms()) {
       const int rc = run_decode_stream_linear(a, stream);
@@ -238,8 +253,10 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
   // Prefill: the weight tile dequantised into tensor memory -- one CTA per
   // 128 rows (K split over a cluster when the tiles are few) for problems
   // that 256 x 256 pair tiles would leave mostly idle, CTA pairs otherwise.
+  // Groups of 32 columns (two per 64-column k-block) take the one-CTA kernel.
   const TsPlan tp = prefill_ts_plan(a.fmt, a.M, a.K, a.N);
   if (tp.tokens_per_tile > 0) return run_prefill_ts_linear(a, tp, stream);
+  if (a.fmt == 0 && a.group_size < 64) return run_prefill_ts_linear(a, TsPlan{128, 1}, stream);
   return run_prefill_ts2_linear(a, stream);
 }
 
@@ -252,7 +269,8 @@ int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
   if (M < 0 || K <= 0 || N <= 0 || M > kIntMax || K > kIntMax || N > kIntMax) return NSQ_EINVAL;
   if (!valid_act_dtype(x_dtype) || !valid_bias_dtype(bias_dtype)) return NSQ_EINVAL;
   if ((bias_dtype == NSQ_DTYPE_NONE) != (bias == nullptr)) return NSQ_EINVAL;
-  if (group_size <= 0 || group_size % 128 != 0) return NSQ_ENOTSUP;
+  // groups of 32, 64 or any multiple of 128 columns (the reference accepts any size)
+  if (!(group_size == 32 || group_size == 64 || (group_size > 0 && group_size % 128 == 0))) return NSQ_ENOTSUP;
   if (K % 32 != 0) return NSQ_ENOTSUP;  // qweight rows must be a 16-byte multiple for TMA
   if (M == 0) return NSQ_OK;
   if (!x || !qweight || !scales || !zeros || !y) return NSQ_EINVAL;
@@ -318,7 +336,9 @@ static int fused_common(int fmt, int mode, const void* x, int x_dtype, int64_t M
   if (!valid_act_dtype(x_dtype) || !valid_bias_dtype(bias_dtype)) return NSQ_EINVAL;
   if (!w || !ns || (fmt == 0 && (!scales || !zeros)) || (fmt == 1 && !wscales)) return NSQ_EINVAL;
   if ((bias_dtype == NSQ_DTYPE_NONE) != (biases == nullptr)) return NSQ_EINVAL;
-  if (fmt == 0 && (group_size <= 0 || group_size % 128 != 0)) return NSQ_ENOTSUP;
+  if (fmt == 0 && !(group_size == 32 || group_size == 64 || (group_size > 0 && group_size % 128 == 0))) {
+    return NSQ_ENOTSUP;
+  }
   if (K % (fmt == 0 ? 32 : 16) != 0) return NSQ_ENOTSUP;  // 16-byte row pitch of the weights for TMA
   if (M > 32) return NSQ_ENOTSUP;                         // decode batches only: call the single linears
   int64_t cols = 0;

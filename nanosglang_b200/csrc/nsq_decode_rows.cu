@@ -34,6 +34,7 @@
 
 #include "nsq_common.cuh"
 #include "nsq_internal.h"
+#include "nsq_tmem_operand.cuh"
 
 namespace nsq {
 
@@ -79,6 +80,7 @@ struct RowsParams {
   int R, KW;          // row groups per CTA (most), warps per row group
   int bias_dtype;
   int mode;           // 0: y[:, seg] = x W_seg^T; 1: y = SiLU(x Wg^T) * (x Wu^T), seg 0 gate, seg 1 up
+  int small_group;    // AWQ groups of 32 / 64 columns: dequantise before the MMA
   int nsegs;
   RowsSeg seg[3];
   int rows_half;      // smem rows of one weight half-box region (16 R)
@@ -334,7 +336,9 @@ __global__ void __launch_bounds__(kThreadsRows, 1) decode_rows_kernel(const __gr
       nsz_a[j] = nsz_b[j] = 0u;
       const int kk = st * F::kSK + j * F::kPieceK;
       if (FMT == 0 && active && st < p.nstage && (j % KW) == kw && kk < p.K) {
-        const int gi = kk / p.group_size;
+        // this thread's 32 columns of the piece lie in one group for groups of
+        // 32, 64 and multiples of 128
+        const int gi = (p.small_group ? kk + 32 * c : kk) / p.group_size;
         if (va) nsz_a[j] = (uint32_t)__ldg(sca + (int64_t)n_a * p.G + gi) | ((uint32_t)__ldg(zra + (int64_t)n_a * p.G + gi) << 16);
         if (vb) nsz_b[j] = (uint32_t)__ldg(scb + (int64_t)n_b * p.G + gi) | ((uint32_t)__ldg(zrb + (int64_t)n_b * p.G + gi) << 16);
       }
@@ -369,6 +373,33 @@ __global__ void __launch_bounds__(kThreadsRows, 1) decode_rows_kernel(const __gr
         const uint32_t wh[4] = {wbv.x, wbv.y, wbv.z, wbv.w};
         const uint32_t xrow = sbase + xoff_j[jj];  // this thread's x row (token g) in the piece's first box
         if constexpr (FMT == 0) {
+          if (p.small_group) {
+            // groups of 32 / 64: every thread's columns carry their own scale,
+            // so the weights are dequantised before the MMA (as the prefill
+            // converters do) and accumulate straight into acc
+            const TsRowDq<BF16> rpa = ts_row_dq<BF16>(sa[j], za[j]);
+            const TsRowDq<BF16> rpb = ts_row_dq<BF16>(sb[j], zb[j]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t eg[4], eh[4];
+              unpack_nibble_pairs<BF16>(wg[i], eg);
+              unpack_nibble_pairs<BF16>(wh[i], eh);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                eg[t] = ts_dq2<BF16>(eg[t], rpa);
+                eh[t] = ts_dq2<BF16>(eh[t], rpb);
+              }
+              const uint32_t a0[4] = {eg[0], eh[0], eg[1], eh[1]};
+              const uint32_t a1[4] = {eg[2], eh[2], eg[3], eh[3]};
+#pragma unroll
+              for (int jt = 0; jt < MT; ++jt) {
+                const uint4 v = lds128(xrow + xq[i] + jt * 1024);
+                mma_16816<BF16>(acc[jt], a0, prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632));
+                mma_16816<BF16>(acc[jt], a1, prmt(v.y, v.w, 0x5410), prmt(v.y, v.w, 0x7632));
+              }
+            }
+            continue;
+          }
           float part[MT][4];
 #pragma unroll
           for (int jt = 0; jt < MT; ++jt) part[jt][0] = part[jt][1] = part[jt][2] = part[jt][3] = 0.f;
@@ -563,7 +594,7 @@ cudaError_t dispatch_rows(int mt, const CUtensorMap& xmap, const RowsMaps& maps,
 int run_decode_rows(const RowsLaunch& L, cudaStream_t stream) {
   const int M = L.M, K = L.K;
   if (M <= 0 || M > 32 || L.nw < 1 || L.nw > 3 || (L.mode == 1 && L.nw != 2)) return NSQ_ENOTSUP;
-  if (L.fmt == 0 && L.group_size % 128 != 0) return NSQ_ENOTSUP;
+  if (L.fmt == 0 && !(L.group_size == 32 || L.group_size == 64 || L.group_size % 128 == 0)) return NSQ_ENOTSUP;
   const int mt = (M + 7) / 8;
   const int mpad = mt * 8;
   const int rowpg = L.mode == 0 ? 16 : 8;
@@ -618,6 +649,7 @@ int run_decode_rows(const RowsLaunch& L, cudaStream_t stream) {
   p.nstage = (K + SK - 1) / SK;
   p.bias_dtype = L.bias_dtype;
   p.mode = L.mode;
+  p.small_group = L.fmt == 0 && L.group_size < 128 ? 1 : 0;
   p.rows_half = 16 * p.R;
   const int wbytes = 2 * p.rows_half * 128;
   p.xoff = wbytes;

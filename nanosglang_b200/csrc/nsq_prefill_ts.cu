@@ -321,12 +321,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
     // register ring so their latency hides behind whole groups of k-blocks
     const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
     const unsigned short* zr16 = reinterpret_cast<const unsigned short*>(p.zeros);
+    // Groups of 32 columns: this thread's 32 columns of k-block kb are group
+    // 2 kb + half, so it walks every other group; larger groups span whole
+    // k-blocks and both halves share them.
+    const int gstep = p.group_size < BK ? BK / p.group_size : 1;
     int pu = blockIdx.x, pg = 0, pg_hi = 0;
     auto unit_groups = [&](int u, int& glo, int& ghi) {
       int lo, hi;
       unit_kb(u, lo, hi);
-      glo = (lo * BK) / p.group_size;
-      ghi = hi > lo ? ((hi - 1) * BK) / p.group_size + 1 : glo;
+      if (gstep > 1) {
+        glo = lo * gstep + (half * 32) / p.group_size;
+        ghi = hi * gstep;
+      } else {
+        glo = (lo * BK) / p.group_size;
+        ghi = hi > lo ? ((hi - 1) * BK) / p.group_size + 1 : glo;
+      }
     };
     if (pu < num_units) unit_groups(pu, pg, pg_hi);
     auto load_sz = [&]() -> uint32_t {
@@ -339,11 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_ts_kernel(
         int wt, tt;
         unit_tile(pu, wt, tt);
         const int n = wt * BW + row;
-        if (n < p.N) {
+        if (n < p.N && pg < p.G) {  // (a half past K in the last k-block has no group)
           const int64_t off = (int64_t)n * p.G + pg;
           v = (uint32_t)__ldg(sc16 + off) | ((uint32_t)__ldg(zr16 + off) << 16);
         }
-        ++pg;
+        pg += gstep;
       }
       return v;
     };

@@ -196,6 +196,34 @@ def test_awq_linear_decode_large_layer(m):
     assert err <= GEMM_TOL, err
 
 
+@pytest.mark.parametrize("gs", [32, 64])
+@pytest.mark.parametrize("m", [1, 16, 32, 48, 100, 1000])
+@pytest.mark.parametrize("n,k,zm", [(4864, 896, "int"), (1000, 1056, "frac"), (4096, 4096, "int")])
+def test_awq_linear_small_groups(gs, m, n, k, zm):
+    """Groups of 32 and 64 columns (the reference takes any group size,
+    quantization.py:93-124): row-streaming decode kernel up to 32 tokens,
+    one-CTA tcgen05 kernel above; K = 1056 leaves half a 64-column k-block."""
+    err = _awq_case(m, n, k, gs, torch.bfloat16, bias=(m == 16), zm=zm, seed=gs + m + n)
+    assert err <= GEMM_TOL, err
+
+
+def test_quantize_model_group_64_forward():
+    """quantize_model(..., group_size=64) gives working modules (bit-exact
+    quantiser, forward against the fp32 oracle of the quantised weight)."""
+    from nanosglang_b200 import quantization as Q
+    torch.manual_seed(4)
+    model = nn.Sequential(nn.Linear(512, 768, bias=True), nn.Linear(768, 512)).cuda()
+    Q.quantize_model(model, "awq", 64)
+    for mod in model:
+        assert isinstance(mod, Q.AWQLinear) and mod.group_size == 64
+    for m in (4, 40, 300):
+        x = torch.randn(m, 512, device="cuda", dtype=torch.bfloat16)
+        mod = model[0]
+        ref = O.awq_linear(_to_np(x), mod.qweight.cpu().numpy(), mod.scales.cpu().numpy(), mod.zeros.cpu().numpy(),
+                           512, 64, mod.bias.detach().float().cpu().numpy())
+        assert O.rel_fro(_to_np(mod(x)), ref) <= GEMM_TOL
+
+
 @pytest.mark.parametrize("m", [65, 128, 200, 1024])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_awq_linear_prefill(m, dtype):
@@ -240,7 +268,7 @@ def test_awq_linear_fp16_matches_reference_forward_golden():
     d = _g("awq_dequant_forward.npz")
     for ci in range(int(d["ncases"][0])):
         n, k, gs = (int(v) for v in d[f"c{ci}_meta"])
-        if gs % 128 or k % 32:
+        if (gs % 128 and gs not in (32, 64)) or k % 32:
             continue
         x = torch.from_numpy(_f16(d[f"c{ci}_x"])).cuda()
         b = torch.from_numpy(_f16(d[f"c{ci}_bias"])).cuda() if f"c{ci}_bias" in d else None
@@ -253,9 +281,9 @@ def test_awq_linear_fp16_matches_reference_forward_golden():
 
 def test_awq_linear_unsupported_group_size_raises():
     from nanosglang_b200 import _lib, ops
-    (_, _, _), (tq, ts, tz) = rand_awq(64, 256, 64, seed=3)
+    (_, _, _), (tq, ts, tz) = rand_awq(64, 384, 96, seed=3)
     with pytest.raises(_lib.NsqError):
-        ops.awq_linear(torch.randn(4, 256, device="cuda", dtype=torch.bfloat16), tq, ts, tz, 64)
+        ops.awq_linear(torch.randn(4, 384, device="cuda", dtype=torch.bfloat16), tq, ts, tz, 96)
 
 
 # ---------------------------------------------------------------------------

@@ -40,7 +40,8 @@ def test_version_and_strerror():
 FAKE = 0x100000  # never dereferenced: validation fails before any device access
 
 
-@pytest.mark.parametrize("k,gs,expect", [(96 + 8, 128, _lib.ENOTSUP), (896, 64, _lib.ENOTSUP), (896, 0, _lib.ENOTSUP)])
+@pytest.mark.parametrize("k,gs,expect", [(96 + 8, 128, _lib.ENOTSUP), (896, 96, _lib.ENOTSUP), (896, 0, _lib.ENOTSUP),
+                                         (896, 48, _lib.ENOTSUP)])
 def test_awq_linear_rejects_unsupported_shapes(k, gs, expect):
     lib = _lib.load()
     rc = lib.nsq_awq_linear(FAKE, _lib.DTYPE_BF16, 4, k, 64, FAKE, FAKE, FAKE, gs, None, _lib.DTYPE_NONE, FAKE,
