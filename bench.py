@@ -264,8 +264,19 @@ def build_gpu_cases(torch, ops, device, rank, world):
             ks = codes.shape[1]
             ns = codes.shape[0]
             x = torch.randn(m, ks, generator=g).to(torch.bfloat16).to(device)
-            cases.append({"name": name, "m": m, "k": k, "n": n, "ks": ks, "ns": ns, "codes": codes,
-                          "scale": scale, "x": x, "row": row})
+            case = {"name": name, "m": m, "k": k, "n": n, "ks": ks, "ns": ns, "codes": codes,
+                    "scale": scale, "x": x, "row": row}
+            if row:
+                # the product's row-parallel layer: local GEMM + all_reduce, chunked
+                # and overlapped on a side stream from 2048 tokens on
+                from nanosglang_b200.quantization import FP8Linear
+                from nanosglang_b200.tensor_parallel import RowParallelLinear
+                with torch.device(device):
+                    shard = FP8Linear(ks, ns)
+                shard.weight_fp8 = codes
+                shard.weight_scale = scale
+                case["rp"] = RowParallelLinear(k, n, world, rank, linear=shard)
+            cases.append(case)
             del w
     return cases
 
@@ -300,9 +311,10 @@ def run_ours(args):
     stream = torch.cuda.Stream(device)
 
     def one_linear(c):
-        out = ops.fp8_linear(c["x"], c["codes"], c["scale"])
         if c["row"]:
-            dist.all_reduce(out)
+            out = c["rp"](c["x"])
+        else:
+            out = ops.fp8_linear(c["x"], c["codes"], c["scale"])
         c["y"] = out
         return out
 

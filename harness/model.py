@@ -87,6 +87,11 @@ class RMSNorm(nn.Module):
         residual = residual + x
         return self.forward(residual), residual
 
+    def fast(self, x: torch.Tensor) -> torch.Tensor:
+        """The same normalisation as one fused torch kernel (fp32 inside), for
+        the harness's own decode/prefill paths (fewer launches per step)."""
+        return F.rms_norm(x, (x.shape[-1],), self.weight.to(x.dtype), self.eps)
+
 
 def precompute_rope_freqs(head_dim: int, max_seq_len: int, theta: float, device=None):
     """causal_lm.py:157-164: cos/sin tables (max_seq_len, head_dim/2), float32."""
@@ -94,6 +99,16 @@ def precompute_rope_freqs(head_dim: int, max_seq_len: int, theta: float, device=
     t = torch.arange(max_seq_len, device=device).float()
     freqs = torch.outer(t, freqs)
     return freqs.cos(), freqs.sin()
+
+
+def apply_rope_full(x: torch.Tensor, cos_full: torch.Tensor, sin_full: torch.Tensor, positions: torch.Tensor):
+    """apply_rope with the cos/sin tables already duplicated to head_dim and in
+    x's dtype ((max_seq_len, head_dim)); x is (tokens, heads, dim)."""
+    half = x.shape[-1] // 2
+    c = cos_full[positions].unsqueeze(1)
+    s = sin_full[positions].unsqueeze(1)
+    rotated = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+    return torch.addcmul(x * c, rotated, s)
 
 
 def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, position_ids: torch.Tensor) -> torch.Tensor:
@@ -160,8 +175,8 @@ class Attention(nn.Module):
         q = q.reshape(bs, nh, self.head_dim)
         k = k.reshape(bs, nkv, self.head_dim)
         v = v.reshape(bs, nkv, self.head_dim)
-        q = apply_rope(q, cos, sin, positions)
-        k = apply_rope(k, cos, sin, positions)
+        q = apply_rope_full(q, cos, sin, positions)
+        k = apply_rope_full(k, cos, sin, positions)
         rows = torch.arange(bs, device=hidden_states.device)
         k_cache[rows, :, positions, :] = k
         v_cache[rows, :, positions, :] = v
@@ -233,10 +248,11 @@ class DecoderLayer(nn.Module):
                            attention_mask)
         return self._finish(h, residual)
 
-    def forward_decode(self, hidden_states, cos, sin, positions, k_cache, v_cache, mask):
-        h = self.self_attn.forward_decode(self.input_layernorm(hidden_states), cos, sin, positions, k_cache,
-                                          v_cache, mask)
-        return self._finish(h, hidden_states)
+    def forward_decode(self, hidden_states, cos_full, sin_full, positions, k_cache, v_cache, mask):
+        h = self.self_attn.forward_decode(self.input_layernorm.fast(hidden_states), cos_full, sin_full, positions,
+                                          k_cache, v_cache, mask)
+        residual = hidden_states + h
+        return residual + self.mlp(self.post_attention_layernorm.fast(residual))
 
     def forward_prefill(self, hidden_states, cos, sin, positions, k_cache, v_cache, slot):
         h = self.self_attn.forward_prefill(self.input_layernorm(hidden_states), cos, sin, positions, k_cache,
@@ -265,12 +281,22 @@ class CausalLM(nn.Module):
                       kv_caches[i] if kv_caches is not None else None, cache_position, attention_mask)
         return self.lm_head(self.norm(h))
 
+    def rope_tables(self, dtype):
+        """cos/sin duplicated to head_dim in ``dtype`` (cached), for the decode path."""
+        key = ("rope_full", dtype)
+        if getattr(self, "_rope_key", None) != key:
+            self._rope_full = (torch.cat([self.rope_cos, self.rope_cos], -1).to(dtype),
+                               torch.cat([self.rope_sin, self.rope_sin], -1).to(dtype))
+            self._rope_key = key
+        return self._rope_full
+
     def forward_decode(self, tokens, positions, caches, mask):
         """tokens/positions (bs,), caches [(k, v)] per layer -> logits (bs, vocab)."""
         h = self.embed_tokens(tokens)
+        cos_full, sin_full = self.rope_tables(h.dtype)
         for layer, (kc, vc) in zip(self.layers, caches):
-            h = layer.forward_decode(h, self.rope_cos, self.rope_sin, positions, kc, vc, mask)
-        return self.lm_head(self.norm(h))
+            h = layer.forward_decode(h, cos_full, sin_full, positions, kc, vc, mask)
+        return self.lm_head(self.norm.fast(h))
 
     def forward_prefill(self, tokens, caches, slot):
         """One prompt (seq,) into cache slot ``slot`` -> logits of its last token (vocab,)."""

@@ -16,8 +16,10 @@ dtype:
   row parallel (o, down)  input columns [r*K/tp, (r+1)*K/tp) (qweight words,
         scale/zero groups for AWQ; weight_fp8 columns for FP8), then one
         ``all_reduce(SUM)`` of the partial [M, hidden] output over NCCL on the
-        current stream (graph-capturable). The bias is kept on rank 0 only so
-        it is added exactly once, inside rank 0's GEMM epilogue.
+        current stream (graph-capturable). From 2048 tokens on, the rows are
+        split into four chunks and each chunk's all-reduce runs on a side
+        stream while the next chunk's GEMM runs. The bias is kept on rank 0
+        only so it is added exactly once, inside rank 0's GEMM epilogue.
 """
 
 from __future__ import annotations
@@ -188,6 +190,17 @@ class ColumnParallelLinear(nn.Module):
             self.linear.bias.data.copy_(full_bias[r0:r1])
 
 
+_SIDE_STREAMS = {}
+
+
+def _side_stream(device) -> torch.cuda.Stream:
+    """One side stream per device for the overlapped row-parallel reductions."""
+    key = torch.device(device).index
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = torch.cuda.Stream(device)
+    return _SIDE_STREAMS[key]
+
+
 class RowParallelLinear(nn.Module):
     """Linear split along the input dimension + all-reduce (tensor_parallel.py:108-151).
 
@@ -214,11 +227,45 @@ class RowParallelLinear(nn.Module):
         return cls(module.in_features, module.out_features, world_size, rank, reduce_output=reduce_output,
                    linear=shard)
 
+    # Prefill-sized inputs are split into token chunks so that the all-reduce
+    # of one chunk (on a side stream) runs while the next chunk's GEMM does.
+    overlap_min_tokens = 2048
+    overlap_chunks = 4
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        output = self.linear(x)
-        if self.reduce_output and self.world_size > 1:
+        if not (self.reduce_output and self.world_size > 1):
+            return self.linear(x)
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        m = x2.shape[0]
+        if m < self.overlap_min_tokens or not x2.is_cuda:
+            output = self.linear(x2)
             dist.all_reduce(output, op=dist.ReduceOp.SUM)
-        return output
+            return output.reshape(*lead, output.shape[-1])
+        return self._forward_overlapped(x2).reshape(*lead, -1)
+
+    def _forward_overlapped(self, x2: torch.Tensor) -> torch.Tensor:
+        """GEMM chunk i+1 on the current stream while chunk i is all-reduced on
+        a side stream; the caller's stream waits for the last reduction. Same
+        result as one GEMM + one all_reduce (each output row is reduced once)."""
+        compute = torch.cuda.current_stream(x2.device)
+        side = _side_stream(x2.device)
+        side.wait_stream(compute)
+        m = x2.shape[0]
+        step = (m + self.overlap_chunks - 1) // self.overlap_chunks
+        step = (step + 127) // 128 * 128
+        parts = []
+        for r0 in range(0, m, step):
+            y = self.linear(x2[r0:r0 + step])
+            done = torch.cuda.Event()
+            done.record(compute)
+            side.wait_event(done)
+            with torch.cuda.stream(side):
+                dist.all_reduce(y, op=dist.ReduceOp.SUM)
+            y.record_stream(side)
+            parts.append(y)
+        compute.wait_stream(side)
+        return torch.cat(parts) if len(parts) > 1 else parts[0]
 
     def load_weight_shard(self, full_weight: torch.Tensor, full_bias: Optional[torch.Tensor] = None):
         """Copy this rank's columns of a full dense weight (tensor_parallel.py:142-151);
