@@ -304,6 +304,9 @@ def run_ours(args):
     _lib.set_pdl(not args.no_pdl)
     peaks, peak_src = load_peaks()
 
+    if args.tp_overlap > 0:
+        from nanosglang_b200.tensor_parallel import RowParallelLinear
+        RowParallelLinear.overlap_min_tokens = args.tp_overlap
     cases = build_gpu_cases(torch, ops, device, rank, world)
     for c in cases:
         c["y"] = torch.empty(c["m"], c["ns"], dtype=torch.bfloat16, device=device)
@@ -486,6 +489,8 @@ def run_ours(args):
         tok_s = {"config2": bench_config2_tok_s(torch, dist, device, rank, world, args),
                  "config3": bench_config3_tok_s(torch, dist, device, rank, world, args)}
 
+    host = measure_host_overhead(torch, ops, device) if world == 1 else None
+
     code, where, block = _lib.device_status()
     if code != 0:
         raise RuntimeError(f"device status {code} (tag {where}, block {block})")
@@ -503,7 +508,7 @@ def run_ours(args):
             "config": sweep_config(world),
             "roofline": roofline, "decode_kernel": decode_line, "awq_config0": awq, "cpu_baseline": cpu,
             "e2e": e2e, "gpu_launches": len(cases) * args.steps, "clocks": clocks, "parity": parity,
-            "tok_s": tok_s,
+            "tok_s": tok_s, "host_overhead": host,
         }
         if tp_breakdown is not None:
             out["tp_breakdown"] = tp_breakdown
@@ -511,6 +516,29 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     return out
+
+
+def measure_host_overhead(torch, ops, device):
+    """Host time of one eager FP8Linear.forward call (validation, tensor-map
+    encoding, launch; no synchronisation), per path: what an eager prefill pays
+    per linear outside a CUDA graph. Device work of the calls overlaps."""
+    out = {}
+    g = torch.Generator().manual_seed(5)
+    for name, m, k, n in (("decode M=8 896->4864", 8, 896, 4864), ("prefill M=1024 896->4864", 1024, 896, 4864)):
+        codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(device))
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(device)
+        for _ in range(20):
+            ops.fp8_linear(x, codes, scale)
+        torch.cuda.synchronize()
+        reps = 200
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            ops.fp8_linear(x, codes, scale)
+        t1 = time.perf_counter()
+        torch.cuda.synchronize()
+        out[name] = round((t1 - t0) * 1e6 / reps, 2)
+    return {"us_per_call": out, "note": "host time per eager ops.fp8_linear call (Python wrapper + C ABI + "
+                                        "tensor-map encoding + launch), device not synchronised"}
 
 
 def check_parity(torch, dist, ops, cases, rank, world, device):
@@ -587,9 +615,9 @@ def bench_config2_tok_s(torch, dist, device, rank, world, args):
     U[64, 128], greedy, all requests admitted at once; output tokens / wall
     clock through the harness engine (packed prefill + CUDA-graph decode
     steps), prompts up from pinned host memory and tokens back inside the
-    timed region. At N GPUs: N independent replicas, requests split
-    round-robin (the 14 query / 2 KV heads do not shard 4 or 8 ways), tokens
-    summed, time = the slowest replica."""
+    timed region. At N GPUs: N independent replicas (the 14 query / 2 KV
+    heads do not shard 4 or 8 ways), each serving its own 32-request workload,
+    tokens summed, time = the slowest replica."""
     from harness import engine as E
     from harness import model as H
     cfg = H.QWEN2_5_0_5B
@@ -597,9 +625,9 @@ def bench_config2_tok_s(torch, dist, device, rank, world, args):
     H.quantize_projections_awq(model)
     H.init_awq(model, 2)
     H.fuse_projections(model)  # q/k/v and gate/up+SiLU as one launch each at decode batch sizes
-    prompts, outs = E.make_workload(32, 100, 512, 64, 128, cfg.vocab_size, seed=0)
-    mine = list(range(rank, len(prompts), world))
-    ps, os_ = [prompts[i] for i in mine], [outs[i] for i in mine]
+    # every replica serves the whole 32-request workload (its own seed): the
+    # per-GPU batch stays the configuration's, so N replicas serve N x the work
+    ps, os_ = E.make_workload(32, 100, 512, 64, 128, cfg.vocab_size, seed=rank)
     eng = E.DecodeEngine(model, max_slots=len(ps), max_len=512 + 128 + 8, max_steps=128)
     eng.capture()
     step_ms = E.time_decode_step(eng, len(ps))
@@ -616,13 +644,17 @@ def bench_config2_tok_s(torch, dist, device, rank, world, args):
             el = float(t.item())
         runs.append(el)
     el = statistics.median(runs)
-    total_out = sum(outs)
+    total_out = sum(os_)
+    if world > 1:
+        t = torch.tensor([total_out], device=device, dtype=torch.float64)
+        dist.all_reduce(t)
+        total_out = int(t.item())
     del eng, model
     torch.cuda.empty_cache()
     return {"workload": "config 2: Qwen2.5-0.5B AWQ int4 (all projections), 32 requests, prompt U[100,512], "
                         "output U[64,128], greedy, bf16 activations", "tok_s": round(total_out / el, 1),
             "unit": "output tokens/s (wall clock)", "elapsed_s": round(el, 4), "output_tokens": total_out,
-            "prompt_tokens": sum(len(p) for p in prompts), "replicas": world,
+            "prompt_tokens_per_replica": sum(len(p) for p in ps), "replicas": world, "scaling": "weak",
             "decode_step_ms": round(step_ms, 4), "decode_step_batch": len(ps),
             "method": "packed prefill + one CUDA-graph replay per decode step (harness engine), fused q/k/v and "
                       "gate/up+SiLU launches at decode batch sizes; median of 3 runs after one warm-up"}
@@ -798,6 +830,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle leg")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-model", action="store_true", help="skip the model-level tok/s legs (configs 2 and 3)")
+    ap.add_argument("--tp-overlap", type=int, default=0, metavar="TOKENS",
+                    help="row-parallel layers overlap chunked GEMMs with their all-reduces from this many tokens "
+                         "(0: off, the default)")
     ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0"], default=None,
                     help="run a small case of one kernel class for a profiler capture, then exit")
     args = ap.parse_args()

@@ -203,6 +203,12 @@ int nsq_set_wait_limit_ns(uint64_t ns);
  * in the reference. Not for production use. */
 int nsq_test_withhold_weight_load(int enable);
 
+/* Number of SMs the linear kernels leave free when they size their grids
+ * (default 0; at most half the SMs), so that a collective launched on
+ * another stream can run beside them. Returns the previous setting. No
+ * counterpart in the reference (its all-reduce is serial). */
+int nsq_set_sm_reserve(int n);
+
 /* Opt in (1) or out (0, default) of programmatic dependent launch for the
  * linear kernels: with it on, a linear starts streaming its weights while the
  * previous kernel on the stream drains. Only valid when no kernel earlier on

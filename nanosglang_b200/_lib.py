@@ -63,6 +63,7 @@ SIGNATURES = {
     "nsq_fp8_quantize_noalloc": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
     "nsq_set_pdl": (c_int, [c_int]),
     "nsq_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
+    "nsq_set_sm_reserve": (c_int, [c_int]),
     "nsq_test_withhold_weight_load": (c_int, [c_int]),
 }
 
@@ -123,6 +124,11 @@ def device_status():
 def device_status_reset() -> None:
     """Clear the device status word (also restores the default wait limit)."""
     check(load().nsq_device_status_reset(), "nsq_device_status_reset")
+
+
+def set_sm_reserve(n: int) -> int:
+    """SMs the linear kernels leave free for a concurrent collective; returns the previous value."""
+    return int(load().nsq_set_sm_reserve(int(n)))
 
 
 def set_wait_limit_ns(ns: int) -> None:

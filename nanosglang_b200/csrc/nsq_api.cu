@@ -26,6 +26,7 @@ std::atomic<int> g_arch_ok[kMaxDevices];  // 0 unknown, 1 ok, -1 not sm_100
 std::atomic<DevStatus*> g_status_ptr[kMaxDevices];
 std::atomic<int> g_pdl{0};
 std::atomic<int> g_withhold{0};  // failure-path test hook (nsq_test_withhold_weight_load)
+std::atomic<int> g_sm_reserve{0};  // SMs the linear kernels leave free (nsq_set_sm_reserve)
 
 std::atomic<PFN_cuTensorMapEncodeTiled_v12000> g_encode{nullptr};
 
@@ -71,7 +72,9 @@ int num_sms() {
   if (d < 0) return 148;
   if (g_sms[d].load(std::memory_order_acquire) == 0) check_device();
   const int sms = g_sms[d].load(std::memory_order_acquire);
-  return sms > 0 ? sms : 148;
+  const int all = sms > 0 ? sms : 148;
+  const int use = all - g_sm_reserve.load(std::memory_order_relaxed);
+  return use >= all / 2 ? use : all / 2;
 }
 
 DevStatus* device_status_ptr() {
@@ -173,6 +176,8 @@ int nsq_set_wait_limit_ns(uint64_t ns) {
 }
 
 int nsq_test_withhold_weight_load(int enable) { return g_withhold.exchange(enable ? 1 : 0); }
+
+int nsq_set_sm_reserve(int n) { return g_sm_reserve.exchange(n < 0 ? 0 : n); }
 
 int nsq_awq_dequant(const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
                     uint16_t* w_out, int64_t N, int64_t K, int64_t group_size, void* stream) {

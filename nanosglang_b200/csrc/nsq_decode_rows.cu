@@ -122,6 +122,24 @@ __device__ __forceinline__ uint32_t sw128(uint32_t base, int row, int q) {
   return base + (uint32_t)row * 128u + ((uint32_t)(q ^ (row & 7)) << 4);
 }
 
+// Two e4m3 codes (low byte first) -> f16x2, exact (every e4m3 value is an
+// fp16 value), with the hardware conversion.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t codes16) {
+  uint32_t d;
+  asm("{\n\t.reg .b16 c;\n\tcvt.u16.u32 c, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, c;\n\t}" : "=r"(d) : "r"(codes16));
+  return d;
+}
+
+// bf16 pair -> fp16 pair of the values times 2^-8, rounded to nearest. Exact
+// for |x| in [2^-6, 2^24); smaller values keep the fp16 subnormal precision,
+// which only they lose (their products are below 2^-6 of the weight's).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2_scaled(uint32_t v) {
+  const float lo = __uint_as_float(v << 16) * 0.00390625f;
+  const float hi = __uint_as_float(v & 0xFFFF0000u) * 0.00390625f;
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 template <bool BF16>
 __device__ __forceinline__ float chunk_sum8(const uint4& v) {
   const uint32_t r[4] = {v.x, v.y, v.z, v.w};
@@ -362,6 +380,23 @@ __global__ void __launch_bounds__(kThreadsRows, 1) decode_rows_kernel(const __gr
     }
     if (ok) ok = mbar_wait(&fullw[slot], ph, p.status, 71, abort_flag);
     if (ok) ok = mbar_wait(&fullx[slot], ph, p.status, 72, abort_flag);
+    if constexpr (FMT == 1 && BF16) {
+      // FP8 runs the MMA in fp16: the e4m3 codes convert with one hardware
+      // instruction per pair (the integer route to bf16 takes five). The
+      // stage's bf16 x is rewritten in place as fp16 of x * 2^-8 (scaled back
+      // in the epilogue), every 16-byte chunk once by one consumer thread.
+      if (ok) {
+        const uint32_t xb = smem_u32(smem + (size_t)slot * p.stage_bytes + p.xoff);
+        constexpr int kChunks = kXBoxes * MPAD * 8;
+        for (int i = threadIdx.x; i < kChunks; i += ncw * 32) {
+          const uint4 v = lds128(xb + i * 16);
+          sts128(xb + i * 16, bf16x2_to_f16x2_scaled(v.x), bf16x2_to_f16x2_scaled(v.y),
+                 bf16x2_to_f16x2_scaled(v.z), bf16x2_to_f16x2_scaled(v.w));
+        }
+      }
+      // every consumer warp passes here once per stage, aborted or not
+      named_bar_sync(3, ncw * 32);
+    }
     if (ok && active) {
       const uint32_t sbase = smem_u32(smem + (size_t)slot * p.stage_bytes);
 #pragma unroll
@@ -469,11 +504,11 @@ __global__ void __launch_bounds__(kThreadsRows, 1) decode_rows_kernel(const __gr
             for (int jt = 0; jt < MT; ++jt) xv[jt] = lds128(xrow + xq[h] + jt * 1024);
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
-              uint32_t a[4];
-              e4m3x4_to_pairs<BF16>(wg[2 * h + u], a[0], a[2]);
-              e4m3x4_to_pairs<BF16>(wh[2 * h + u], a[1], a[3]);
+              const uint32_t wgu = wg[2 * h + u], whu = wh[2 * h + u];
+              const uint32_t a[4] = {e4m3x2_to_f16x2(wgu & 0xFFFFu), e4m3x2_to_f16x2(whu & 0xFFFFu),
+                                     e4m3x2_to_f16x2(wgu >> 16), e4m3x2_to_f16x2(whu >> 16)};
 #pragma unroll
-              for (int jt = 0; jt < MT; ++jt) mma_16816<BF16>(acc[jt], a, u ? xv[jt].z : xv[jt].x, u ? xv[jt].w : xv[jt].y);
+              for (int jt = 0; jt < MT; ++jt) mma_16816<false>(acc[jt], a, u ? xv[jt].z : xv[jt].x, u ? xv[jt].w : xv[jt].y);
             }
           }
         }
@@ -510,8 +545,9 @@ __global__ void __launch_bounds__(kThreadsRows, 1) decode_rows_kernel(const __gr
     }
   }
   if (active && kw == 0) {
-    const float ws_a = (FMT == 1) ? __ldg(Sa.wscale) : 1.0f;
-    const float ws_b = (FMT == 1) ? __ldg(Sb.wscale) : 1.0f;
+    constexpr float kXScale = (FMT == 1 && BF16) ? 256.0f : 1.0f;  // undo the 2^-8 of the fp16 x
+    const float ws_a = (FMT == 1) ? __ldg(Sa.wscale) * kXScale : 1.0f;
+    const float ws_b = (FMT == 1) ? __ldg(Sb.wscale) * kXScale : 1.0f;
     float ba = 0.f, bb = 0.f;
     if (p.bias_dtype != NSQ_DTYPE_NONE) {
       if (va && Sa.bias) ba = load_bias(Sa.bias, p.bias_dtype, n_a);

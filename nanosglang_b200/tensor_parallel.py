@@ -16,9 +16,9 @@ dtype:
   row parallel (o, down)  input columns [r*K/tp, (r+1)*K/tp) (qweight words,
         scale/zero groups for AWQ; weight_fp8 columns for FP8), then one
         ``all_reduce(SUM)`` of the partial [M, hidden] output over NCCL on the
-        current stream (graph-capturable). From 2048 tokens on, the rows are
-        split into four chunks and each chunk's all-reduce runs on a side
-        stream while the next chunk's GEMM runs. The bias is kept on rank 0
+        current stream (graph-capturable). Opt-in (``overlap_min_tokens``):
+        the rows are split into chunks and each chunk's all-reduce runs on a
+        side stream while the next chunk's GEMM runs. The bias is kept on rank 0
         only so it is added exactly once, inside rank 0's GEMM epilogue.
 """
 
@@ -227,10 +227,14 @@ class RowParallelLinear(nn.Module):
         return cls(module.in_features, module.out_features, world_size, rank, reduce_output=reduce_output,
                    linear=shard)
 
-    # Prefill-sized inputs are split into token chunks so that the all-reduce
-    # of one chunk (on a side stream) runs while the next chunk's GEMM does.
-    overlap_min_tokens = 2048
+    # Opt-in: prefill-sized inputs split into token chunks, the all-reduce of
+    # one chunk (on a side stream) running while the next chunk's GEMM does,
+    # with the GEMMs leaving `overlap_sm_reserve` SMs free for the collective.
+    # Off by default (overlap_min_tokens = None): on B200 with NCCL, the
+    # serial GEMM + all_reduce was faster on the measured shapes.
+    overlap_min_tokens = None
     overlap_chunks = 4
+    overlap_sm_reserve = 24
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not (self.reduce_output and self.world_size > 1):
@@ -238,7 +242,7 @@ class RowParallelLinear(nn.Module):
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1])
         m = x2.shape[0]
-        if m < self.overlap_min_tokens or not x2.is_cuda:
+        if self.overlap_min_tokens is None or m < self.overlap_min_tokens or not x2.is_cuda:
             output = self.linear(x2)
             dist.all_reduce(output, op=dist.ReduceOp.SUM)
             return output.reshape(*lead, output.shape[-1])
@@ -255,17 +259,26 @@ class RowParallelLinear(nn.Module):
         step = (m + self.overlap_chunks - 1) // self.overlap_chunks
         step = (step + 127) // 128 * 128
         parts = []
-        for r0 in range(0, m, step):
-            y = self.linear(x2[r0:r0 + step])
-            done = torch.cuda.Event()
-            done.record(compute)
-            side.wait_event(done)
-            with torch.cuda.stream(side):
-                dist.all_reduce(y, op=dist.ReduceOp.SUM)
-            y.record_stream(side)
-            parts.append(y)
+        from . import _lib
+        prev = _lib.set_sm_reserve(self.overlap_sm_reserve)
+        try:
+            for r0 in range(0, m, step):
+                parts.append(self._chunk(x2[r0:r0 + step], compute, side))
+        finally:
+            _lib.set_sm_reserve(prev)
         compute.wait_stream(side)
         return torch.cat(parts) if len(parts) > 1 else parts[0]
+
+    def _chunk(self, xc, compute, side):
+        """GEMM of one token chunk on the compute stream; its all-reduce on the side stream."""
+        y = self.linear(xc)
+        done = torch.cuda.Event()
+        done.record(compute)
+        side.wait_event(done)
+        with torch.cuda.stream(side):
+            dist.all_reduce(y, op=dist.ReduceOp.SUM)
+        y.record_stream(side)
+        return y
 
     def load_weight_shard(self, full_weight: torch.Tensor, full_bias: Optional[torch.Tensor] = None):
         """Copy this rank's columns of a full dense weight (tensor_parallel.py:142-151);
@@ -280,9 +293,12 @@ class RowParallelLinear(nn.Module):
 class TPAttention(nn.Module):
     """Container of the sharded attention projections (tensor_parallel.py:154-203).
 
-    As in the reference, the attention computation itself belongs to the
-    model; ``tensor_parallel_model`` shards the projections of an existing
-    attention module in place instead of using this class's forward.
+    Kept for API compatibility with the reference, which also leaves its
+    forward unimplemented: the attention computation belongs to the model,
+    and ``tensor_parallel_model`` shards the projections of an existing
+    attention module in place (and sets its per-rank head counts) instead of
+    replacing it with this class. Its projections are usable directly
+    (``q_proj`` .. ``o_proj`` are Column/RowParallelLinear).
     """
 
     def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: int, head_dim: int, world_size: int,

@@ -112,13 +112,13 @@ def _worker(rank, port, q):
             h = O.bf16_round((g / (1.0 + np.exp(-g))) * u)  # the kernel reads bf16 activations
             ref = O.awq_linear(h, dq, dsc, dz, n, gs)
             res[f"awq_mlp_m{m_tok}"] = O.rel_fro(_bf16_np(y), ref)
-        # prefill-sized row-parallel input: chunked GEMMs with the all-reduces
-        # overlapped on a side stream (RowParallelLinear.overlap_min_tokens)
+        # prefill-sized row-parallel input with the opt-in overlap: chunked GEMMs
+        # with the all-reduces on a side stream (RowParallelLinear.overlap_min_tokens)
         row8, (codes, scale) = _fp8_full(k, n, seed=8)
         xr = torch.randn(4096, n, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
         c0, c1 = O.row_shard_cols(n, WS, rank)
         rp = TP.RowParallelLinear.from_linear(row8, WS, rank)
-        assert 4096 >= rp.overlap_min_tokens
+        rp.overlap_min_tokens = 2048  # opt in for this layer
         y = rp(xr[:, c0:c1].contiguous().cuda())
         res["fp8_row_overlapped_m4096"] = O.rel_fro(_bf16_np(y), O.fp8_linear(xr.float().numpy(), codes, scale))
         torch.cuda.synchronize()
