@@ -713,11 +713,41 @@ def bench_config3_tok_s(torch, dist, device, rank, world, args):
         ms = float(t.item())
     wbytes = sum(b.numel() * b.element_size() for n, b in model.named_buffers()
                  if n.endswith(("qweight", "scales", "zeros")))
+    ar_ms = None
+    if world > 1:
+        # the step's 2 x 32 row-parallel all-reduces of [64, 4096] bf16 alone, as one graph
+        bufs = [torch.zeros(streams, cfg.hidden_size, device=device, dtype=torch.bfloat16)
+                for _ in range(2 * cfg.num_hidden_layers)]
+        s2 = torch.cuda.Stream(device)
+        with torch.cuda.stream(s2):
+            for b in bufs:
+                dist.all_reduce(b)
+        torch.cuda.synchronize()
+        g_ar = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_ar, stream=s2):
+            for b in bufs:
+                dist.all_reduce(b)
+        for _ in range(3):
+            g_ar.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s_ev.record()
+        for _ in range(steps):
+            g_ar.replay()
+        e_ev.record()
+        torch.cuda.synchronize()
+        ar_ms = s_ev.elapsed_time(e_ev) / steps
+        t = torch.tensor([ar_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ar_ms = float(t.item())
+        del g_ar, bufs
     del gph, eng, model
     torch.cuda.empty_cache()
     return {"workload": "config 3: Llama-3-8B AWQ int4, 64 streams at context 2048, bf16 activations",
             "tok_s": round(streams / (ms * 1e-3), 1), "unit": "tokens/s (device time of decode steps)",
             "ms_per_step": round(ms, 4), "tp": world, "awq_weight_bytes_per_rank": int(wbytes),
+            "allreduce_ms_per_step": None if ar_ms is None else round(ar_ms, 4),
+            "allreduce_share": None if ar_ms is None else round(ar_ms / ms, 3),
             "method": f"{steps} replays of the batch-64 decode-step graph, max over ranks"}
 
 
