@@ -120,13 +120,22 @@ __device__ __forceinline__ void issue_x_copy(const DecodeParams& p, uint32_t xbu
   const int cpr = np * F::kChunksPerPiece;  // 16-byte chunks per token row
   const int total = MPAD * cpr;
   const uint16_t* x = static_cast<const uint16_t*>(p.x);
-  for (int idx = tid; idx < total; idx += blockDim.x) {
-    const int t = idx / cpr;
-    const int q = idx - t * cpr;
+  // (t, q) of chunk idx, advanced by the stride instead of divided each time
+  // (this loop runs after the wait, on the launch's critical path)
+  const int nthr = blockDim.x;
+  const int dt = nthr / cpr, dq = nthr - dt * cpr;
+  int t = tid / cpr, q = tid - (tid / cpr) * cpr;
+  for (int idx = tid; idx < total; idx += nthr) {
     const int k = kc0 + q * 8;
     const bool valid = t < p.M && k < p.K;
     const uint16_t* src = valid ? x + (int64_t)t * p.K + k : x;
     cp_async16(xbuf + t * p.xrs + x_swz<FMT>(q, t) * 16, src, valid ? 16u : 0u);
+    t += dt;
+    q += dq;
+    if (q >= cpr) {
+      q -= cpr;
+      ++t;
+    }
   }
 }
 
@@ -190,9 +199,14 @@ template <bool BF16, int MT, bool INT_Z>
 __device__ __forceinline__ void awq_piece(float (&acc)[MT][4], const uint4& wa, const uint4& wb,
                                           uint32_t xrow0, int xrs, const float* xs, float s0, float zb0,
                                           float s1, float zb1, int g, int c) {
-  float part[MT][4];
+  // two accumulator sets (first and second k16 step of each word), so the
+  // MMA dependency chains are 4 long instead of 8 (up to 32 tokens)
+  float part[MT][4], part2[MT][4];
 #pragma unroll
-  for (int jt = 0; jt < MT; ++jt) part[jt][0] = part[jt][1] = part[jt][2] = part[jt][3] = 0.f;
+  for (int jt = 0; jt < MT; ++jt) {
+    part[jt][0] = part[jt][1] = part[jt][2] = part[jt][3] = 0.f;
+    part2[jt][0] = part2[jt][1] = part2[jt][2] = part2[jt][3] = 0.f;
+  }
   const uint32_t wg[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t wh[4] = {wb.x, wb.y, wb.z, wb.w};
   uint32_t z2g = 0, z2h = 0;
@@ -222,11 +236,17 @@ __device__ __forceinline__ void awq_piece(float (&acc)[MT][4], const uint4& wa, 
       const uint32_t p0 = prmt(v.x, v.z, 0x5410), p1 = prmt(v.x, v.z, 0x7632);
       const uint32_t p2 = prmt(v.y, v.w, 0x5410), p3 = prmt(v.y, v.w, 0x7632);
       mma_16816<BF16>(part[jt], a0, p0, p1);
-      mma_16816<BF16>(part[jt], a1, p2, p3);
+      if constexpr (MT <= 4) {
+        mma_16816<BF16>(part2[jt], a1, p2, p3);
+      } else {  // more token tiles already give independent chains; keep registers
+        mma_16816<BF16>(part[jt], a1, p2, p3);
+      }
     }
   }
 #pragma unroll
   for (int jt = 0; jt < MT; ++jt) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) part[jt][e] += part2[jt][e];
     if constexpr (INT_Z) {
       acc[jt][0] = fmaf(s0, part[jt][0], acc[jt][0]);
       acc[jt][1] = fmaf(s0, part[jt][1], acc[jt][1]);
