@@ -676,8 +676,12 @@ def bench_config3_tok_s(torch, dist, device, rank, world, args):
     model = H.build_model(cfg, device=device, dtype=torch.bfloat16)
     H.quantize_projections_awq(model)
     H.init_awq(model, 3)
+    peer = False
     if world > 1:
         TP.tensor_parallel_model(model, world, rank)
+        if args.peer_allreduce:
+            TP.enable_peer_allreduce(4 << 20)  # the step's [64, 4096] bf16 outputs (512 KB) go over NVLink peers
+            peer = True
     H.fuse_projections(model)  # fused launches apply to M <= 32 only; 64 streams keep the separate layers
     eng = E.DecodeEngine(model, max_slots=streams, max_len=ctx + steps + 8, max_steps=steps + 4)
     g = torch.Generator(device=device).manual_seed(4 + rank)
@@ -721,12 +725,12 @@ def bench_config3_tok_s(torch, dist, device, rank, world, args):
         s2 = torch.cuda.Stream(device)
         with torch.cuda.stream(s2):
             for b in bufs:
-                dist.all_reduce(b)
+                TP._all_reduce_sum(b)
         torch.cuda.synchronize()
         g_ar = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_ar, stream=s2):
             for b in bufs:
-                dist.all_reduce(b)
+                TP._all_reduce_sum(b)
         for _ in range(3):
             g_ar.replay()
         torch.cuda.synchronize()
@@ -742,12 +746,17 @@ def bench_config3_tok_s(torch, dist, device, rank, world, args):
         ar_ms = float(t.item())
         del g_ar, bufs
     del gph, eng, model
+    if peer:
+        torch.cuda.synchronize()
+        TP.disable_peer_allreduce()
     torch.cuda.empty_cache()
     return {"workload": "config 3: Llama-3-8B AWQ int4, 64 streams at context 2048, bf16 activations",
             "tok_s": round(streams / (ms * 1e-3), 1), "unit": "tokens/s (device time of decode steps)",
             "ms_per_step": round(ms, 4), "tp": world, "awq_weight_bytes_per_rank": int(wbytes),
             "allreduce_ms_per_step": None if ar_ms is None else round(ar_ms, 4),
             "allreduce_share": None if ar_ms is None else round(ar_ms / ms, 3),
+            "allreduce": ("one-shot NVLink peer all-reduce (nsq_peer_allreduce)" if peer else "NCCL")
+            if world > 1 else None,
             "method": f"{steps} replays of the batch-64 decode-step graph, max over ranks"}
 
 
@@ -860,6 +869,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle leg")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-model", action="store_true", help="skip the model-level tok/s legs (configs 2 and 3)")
+    ap.add_argument("--peer-allreduce", action="store_true",
+                    help="config 3 under TP: reduce the row-parallel outputs with the NVLink peer all-reduce")
     ap.add_argument("--tp-overlap", type=int, default=0, metavar="TOKENS",
                     help="row-parallel layers overlap chunked GEMMs with their all-reduces from this many tokens "
                          "(0: off, the default)")

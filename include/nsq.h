@@ -203,6 +203,32 @@ int nsq_set_wait_limit_ns(uint64_t ns);
  * in the reference. Not for production use. */
 int nsq_test_withhold_weight_load(int enable);
 
+/*
+ * One-shot all-reduce (sum) over NVLink peer memory for tensor parallelism:
+ * the row-parallel all_reduce(SUM) of nano_sglang/distributed/
+ * tensor_parallel.py:134-140 for outputs of at most `max_bytes`. Set-up (not
+ * in the launch path): every rank allocates one workspace of
+ * nsq_peer_workspace_size(world, max_bytes) bytes with
+ * nsq_peer_workspace_alloc (zeroed), exports it with nsq_ipc_handle (64
+ * bytes), and opens every other rank's handle with nsq_ipc_open.
+ * nsq_peer_allreduce(workspaces[world] as mapped in this process, ...) then
+ * sums `in` over the ranks into `out` (may alias `in`): every rank stores its
+ * partial into every workspace, signals, waits (bounded) for the others and
+ * sums the slots in rank order, so every rank gets bit-identical results.
+ * Every rank must make the same sequence of calls. Stream-ordered, no host
+ * synchronisation, graph-capturable. n * sizeof(dtype) must be a multiple of
+ * 16 and at most max_bytes (else NSQ_EALIGN / NSQ_EWORKSPACE). A rank whose
+ * wait runs out records NSQ_EDEVICE_TIMEOUT (tag 90) and returns.
+ */
+size_t nsq_peer_workspace_size(int world, int64_t max_bytes);
+int nsq_peer_workspace_alloc(size_t bytes, void** ptr_out);
+int nsq_peer_workspace_free(void* ptr);
+int nsq_ipc_handle(const void* dev_ptr, void* handle_out);
+int nsq_ipc_open(const void* handle, void** dev_ptr_out);
+int nsq_ipc_close(void* dev_ptr);
+int nsq_peer_allreduce(void* const* workspaces, int rank, int world, int64_t max_bytes, const void* in, void* out,
+                       int64_t n, int dtype, void* stream);
+
 /* Number of SMs the linear kernels leave free when they size their grids
  * (default 0; at most half the SMs), so that a collective launched on
  * another stream can run beside them. Returns the previous setting. No

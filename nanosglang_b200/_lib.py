@@ -64,6 +64,13 @@ SIGNATURES = {
     "nsq_set_pdl": (c_int, [c_int]),
     "nsq_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
     "nsq_set_sm_reserve": (c_int, [c_int]),
+    "nsq_peer_workspace_size": (c_size_t, [c_int, c_int64]),
+    "nsq_peer_workspace_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p)]),
+    "nsq_peer_workspace_free": (c_int, [c_void_p]),
+    "nsq_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "nsq_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "nsq_ipc_close": (c_int, [c_void_p]),
+    "nsq_peer_allreduce": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "nsq_test_withhold_weight_load": (c_int, [c_int]),
 }
 

@@ -36,7 +36,8 @@ from .quantization import AWQLinear, FP8Linear
 
 __all__ = [
     "init_distributed", "ColumnParallelLinear", "RowParallelLinear", "TPAttention", "TPMLP",
-    "tensor_parallel_model", "shard_linear_rows", "shard_linear_cols",
+    "tensor_parallel_model", "shard_linear_rows", "shard_linear_cols", "enable_peer_allreduce",
+    "disable_peer_allreduce",
 ]
 
 
@@ -191,6 +192,32 @@ class ColumnParallelLinear(nn.Module):
 
 
 _SIDE_STREAMS = {}
+_PEER = None  # a peer.PeerAllReduce once enable_peer_allreduce() ran
+
+
+def enable_peer_allreduce(max_bytes: int = 4 << 20, group=None):
+    """Reduce row-parallel outputs of at most ``max_bytes`` with the one-shot
+    NVLink peer all-reduce (nanosglang_b200.peer) instead of NCCL; larger ones
+    keep ``dist.all_reduce``. Collective: every rank calls it once."""
+    global _PEER
+    from .peer import PeerAllReduce
+    if _PEER is None:
+        _PEER = PeerAllReduce(max_bytes=max_bytes, group=group)
+    return _PEER
+
+
+def disable_peer_allreduce():
+    """Back to NCCL for every row-parallel output (collective)."""
+    global _PEER
+    if _PEER is not None:
+        _PEER.close()
+        _PEER = None
+
+
+def _all_reduce_sum(t: torch.Tensor) -> None:
+    if _PEER is not None and _PEER.reduce_(t):
+        return
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
 
 
 def _side_stream(device) -> torch.cuda.Stream:
@@ -244,7 +271,7 @@ class RowParallelLinear(nn.Module):
         m = x2.shape[0]
         if self.overlap_min_tokens is None or m < self.overlap_min_tokens or not x2.is_cuda:
             output = self.linear(x2)
-            dist.all_reduce(output, op=dist.ReduceOp.SUM)
+            _all_reduce_sum(output)
             return output.reshape(*lead, output.shape[-1])
         return self._forward_overlapped(x2).reshape(*lead, -1)
 
