@@ -35,6 +35,7 @@ JSON), for Nsight Compute captures of a small case (one kernel, <= 4 launches):
   prefill        FP8 gate shape, M=16384 (paired-CTA TMEM-operand GEMM), 3 launches
   down8192       FP8 down 4864->896 at M=8192 (the sweep's paired-kernel launch), 3 launches
   awq0           config-0 AWQ linear (M=16, K=896, N=9728), 4 launches
+  awq_llama_gate / fp8_llama_gate   Llama-3-8B gate 4096->14336 at M=16, 3 launches
 """
 
 from __future__ import annotations
@@ -844,6 +845,21 @@ def run_ncu_case(name):
         x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
         for _ in range(3):
             ops.fp8_linear(x, codes, scale)
+    elif name in ("awq_llama_gate", "fp8_llama_gate"):
+        # Llama-3-8B gate 4096 -> 14336 at M = 16, 3 launches (the decode kernel the library picks)
+        m, k, n, gs = 16, 4096, 14336, 128
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        if name == "awq_llama_gate":
+            qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), generator=g, dtype=torch.int64).to(torch.int32)
+            s = (torch.rand(n, k // gs, generator=g) * 0.009 + 0.001).half()
+            z = torch.randint(0, 16, (n, k // gs), generator=g).half()
+            qw, s, z = qw.to(dev), s.to(dev), z.to(dev)
+            for _ in range(3):
+                ops.awq_linear(x, qw, s, z, gs)
+        else:
+            codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
+            for _ in range(3):
+                ops.fp8_linear(x, codes, scale)
     elif name == "awq0":
         m, k, n, gs = 16, 896, 9728, 128
         for _ in range(4):
@@ -874,7 +890,8 @@ def main():
     ap.add_argument("--tp-overlap", type=int, default=0, metavar="TOKENS",
                     help="row-parallel layers overlap chunked GEMMs with their all-reduces from this many tokens "
                          "(0: off, the default)")
-    ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0"], default=None,
+    ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0", "awq_llama_gate", "fp8_llama_gate"],
+                    default=None,
                     help="run a small case of one kernel class for a profiler capture, then exit")
     args = ap.parse_args()
     if args.ncu_case:

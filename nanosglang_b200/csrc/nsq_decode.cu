@@ -43,7 +43,7 @@ namespace nsq {
 namespace {
 
 constexpr int kRowWarps = 4;       // row groups of 16 rows per CTA
-constexpr int kMaxKGroups = 4;     // warps per row group splitting K (intra-CTA split-K)
+constexpr int kMaxKGroups = 2;     // warps per row group splitting K (intra-CTA split-K)
 constexpr int kMaxThreads = kRowWarps * kMaxKGroups * 32;
 constexpr int kRows = 64;          // output rows per CTA
 constexpr int kMaxSlabs = 16;      // TMA boxes per row group (one barrier each)
@@ -289,9 +289,7 @@ __device__ __forceinline__ void fp8_piece(float (&acc)[MT][4], const uint4& wa, 
   }
 }
 
-// KWMAX: the most warps per row group the instantiation is launched with (2,
-// or 4 for up to 16 tokens: 16 warps in at most 64 registers, still two CTAs
-// per SM, so the next launch's CTAs fit beside this one).
+// KWMAX: the most warps per row group the instantiation is launched with.
 template <int FMT, bool BF16, int MT, int KWMAX>
 __global__ void __launch_bounds__(kRowWarps * KWMAX * 32, 2) decode_linear_kernel(
     const __grid_constant__ CUtensorMap wmap, const DecodeParams p) {
@@ -575,10 +573,9 @@ Plan make_plan(int M, int K, int N) {
   pl.nslab = nslab;
   if (nslab > kMaxSlabs) pl.ok = false;
   // two warps per row group when each can keep at least two pieces
-  // (four for up to 16 tokens with at least six pieces: the piece loop is
-  // latency-bound at two warps per SMSP, so more warps shorten it)
+  // (four warps per row group, 64 registers each, measured slower on B200:
+  // config 0 6.3 -> 7.4 us per linear)
   pl.kw = per >= 4 ? 2 : 1;
-  if (M <= 16 && per >= 6) pl.kw = 4;
   // x staging: one buffer for the whole slice if it fits, else two chunk buffers
   const int piece_token_bytes = F::kPieceK * 2;
   int nbuf;
@@ -657,8 +654,8 @@ template <int FMT, bool BF16>
 cudaError_t dispatch_mt(int mt, const CUtensorMap& map, const DecodeParams& p, const Plan& pl,
                         cudaStream_t s) {
   switch (mt) {
-    case 1: return pl.kw > 2 ? launch_t<FMT, BF16, 1, 4>(map, p, pl, s) : launch_t<FMT, BF16, 1, 2>(map, p, pl, s);
-    case 2: return pl.kw > 2 ? launch_t<FMT, BF16, 2, 4>(map, p, pl, s) : launch_t<FMT, BF16, 2, 2>(map, p, pl, s);
+    case 1: return launch_t<FMT, BF16, 1, 2>(map, p, pl, s);
+    case 2: return launch_t<FMT, BF16, 2, 2>(map, p, pl, s);
     case 3: return launch_t<FMT, BF16, 3, 2>(map, p, pl, s);
     case 4: return launch_t<FMT, BF16, 4, 2>(map, p, pl, s);
     case 5: return launch_t<FMT, BF16, 5, 2>(map, p, pl, s);
