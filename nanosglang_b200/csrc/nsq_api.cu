@@ -99,9 +99,47 @@ bool test_withhold() { return g_withhold.load(std::memory_order_relaxed) != 0; }
 
 int device_ready() { return check_device(); }
 
+namespace {
+// Per-thread cache of encoded tensor maps: an eager forward encodes the same
+// maps (same weight, same x buffer from the caching allocator) call after
+// call. The key is every input of the encoding, so a hit is exactly what the
+// driver would return.
+struct MapKey {
+  uint64_t base, inner, outer, stride;
+  uint32_t box_inner, box_outer;
+  int dtype, swizzle;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && inner == o.inner && outer == o.outer && stride == o.stride &&
+           box_inner == o.box_inner && box_outer == o.box_outer && dtype == o.dtype && swizzle == o.swizzle;
+  }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kMapCache = 64;
+thread_local MapEntry t_map_cache[kMapCache];
+
+inline uint32_t map_slot(const MapKey& k) {
+  uint64_t h = k.base * 0x9E3779B97F4A7C15ull ^ (k.inner * 0xC2B2AE3D27D4EB4Full) ^ (k.outer << 17) ^
+               (k.stride << 7) ^ ((uint64_t)k.box_inner << 40) ^ ((uint64_t)k.box_outer << 24) ^
+               ((uint64_t)k.dtype << 56) ^ ((uint64_t)k.swizzle << 60);
+  h ^= h >> 29;
+  return (uint32_t)(h % kMapCache);
+}
+}  // namespace
+
 CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
                               uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  const MapKey key{reinterpret_cast<uint64_t>(base), inner, outer, row_stride_bytes, box_inner, box_outer,
+                   (int)dtype, (int)swizzle};
+  MapEntry& slot = t_map_cache[map_slot(key)];
+  if (slot.valid && slot.key == key) {
+    *map = slot.map;
+    return CUDA_SUCCESS;
+  }
   PFN_cuTensorMapEncodeTiled_v12000 encode = g_encode.load(std::memory_order_acquire);
   if (encode == nullptr) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -122,8 +160,14 @@ CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void*
   const cuuint64_t strides[1] = {row_stride_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  return encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) {
+    slot.key = key;
+    slot.map = *map;
+    slot.valid = true;
+  }
+  return r;
 }
 
 }  // namespace nsq

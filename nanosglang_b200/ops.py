@@ -20,7 +20,15 @@ _ACT_CODES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}
 _BIAS_CODES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
 
 
+try:  # the raw handle of the current stream without building a Stream object (hot path)
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
 def _stream(t: torch.Tensor) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -86,23 +94,37 @@ def awq_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zer
     x: [..., K] fp16 or bf16 (the reference only accepts fp16); returns
     [..., N] in x's dtype.
     """
-    _require_cuda(x, qweight, scales, zeros, bias, what="awq_linear")
-    if x.dtype not in _ACT_CODES:
+    if not (x.is_cuda and qweight.is_cuda and scales.is_cuda and zeros.is_cuda) or (
+            bias is not None and not bias.is_cuda):
+        _require_cuda(x, qweight, scales, zeros, bias, what="awq_linear")
+    code = _ACT_CODES.get(x.dtype)
+    if code is None:
         raise TypeError(f"activation dtype {x.dtype} not supported (float16 / bfloat16)")
-    k = qweight.shape[1] * 8
-    n = qweight.shape[0]
+    n, k8 = qweight.shape
+    k = k8 * 8
     if x.shape[-1] != k:
         raise RuntimeError(f"x has {x.shape[-1]} features, the layer expects {k}")
-    lead = x.shape[:-1]
-    x2 = _aligned(x.reshape(-1, k))
+    if not qweight.is_contiguous() or qweight.data_ptr() & 15:
+        qweight = _aligned(qweight)
+    if not scales.is_contiguous():
+        scales = scales.contiguous()
+    if not zeros.is_contiguous():
+        zeros = zeros.contiguous()
+    x2 = x if x.dim() == 2 else x.reshape(-1, k)
+    if not x2.is_contiguous() or x2.data_ptr() & 15:
+        x2 = _aligned(x2)
     m = x2.shape[0]
-    y = torch.empty(m, n, dtype=x.dtype, device=x.device)
-    b, bcode = _bias_arg(bias)
-    rc = _lib.load().nsq_awq_linear(_ptr(x2), _ACT_CODES[x.dtype], m, k, n, _ptr(_aligned(qweight)),
-                                    _ptr(scales.contiguous()), _ptr(zeros.contiguous()), group_size, _ptr(b),
-                                    bcode, _ptr(y), None, 0, _stream(x))
-    _lib.check(rc, "nsq_awq_linear")
-    return y.reshape(*lead, n)
+    y = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    if bias is None:
+        bptr, bcode = None, _lib.DTYPE_NONE
+    else:
+        b, bcode = _bias_arg(bias)
+        bptr = b.data_ptr()
+    rc = _lib.load().nsq_awq_linear(x2.data_ptr(), code, m, k, n, qweight.data_ptr(), scales.data_ptr(),
+                                    zeros.data_ptr(), group_size, bptr, bcode, y.data_ptr(), None, 0, _stream(x))
+    if rc:
+        _lib.check(rc, "nsq_awq_linear")
+    return y if x.dim() == 2 else y.reshape(*x.shape[:-1], n)
 
 
 def awq_quantize(weight: torch.Tensor, group_size: int = 128):
@@ -172,27 +194,46 @@ def _scale_arg(weight_scale: torch.Tensor) -> torch.Tensor:
     return weight_scale.contiguous()
 
 
+_FP8_TYPES = (torch.float8_e4m3fn, torch.uint8)
+
+
 def fp8_linear(x: torch.Tensor, weight_fp8: torch.Tensor, weight_scale: torch.Tensor,
                bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``FP8Linear.forward`` (quantization.py:49-52): W8A16, the scale is read on
-    the device (no host sync)."""
-    _require_cuda(x, weight_fp8, weight_scale, bias, what="fp8_linear")
-    if x.dtype not in _ACT_CODES:
+    the device (no host sync). Every check is a cheap attribute test on this
+    path (eager prefill pays it per linear); anything unusual takes the
+    general route (copies, errors)."""
+    if not (x.is_cuda and weight_fp8.is_cuda and weight_scale.is_cuda) or (bias is not None and not bias.is_cuda):
+        _require_cuda(x, weight_fp8, weight_scale, bias, what="fp8_linear")
+    code = _ACT_CODES.get(x.dtype)
+    if code is None:
         raise TypeError(f"activation dtype {x.dtype} not supported (float16 / bfloat16)")
-    w = _aligned(_u8(weight_fp8))
+    if weight_fp8.dtype not in _FP8_TYPES:
+        raise TypeError(f"fp8 weight must be float8_e4m3fn, got {weight_fp8.dtype}")
+    w = weight_fp8
+    if not w.is_contiguous() or w.data_ptr() & 15:
+        w = _aligned(w)
     n, k = w.shape
     if x.shape[-1] != k:
         raise RuntimeError(f"x has {x.shape[-1]} features, the layer expects {k}")
-    lead = x.shape[:-1]
-    x2 = _aligned(x.reshape(-1, k))
+    x2 = x if x.dim() == 2 else x.reshape(-1, k)
+    if not x2.is_contiguous() or x2.data_ptr() & 15:
+        x2 = _aligned(x2)
     m = x2.shape[0]
-    y = torch.empty(m, n, dtype=x.dtype, device=x.device)
-    b, bcode = _bias_arg(bias)
-    s = _scale_arg(weight_scale)
-    rc = _lib.load().nsq_fp8_linear(_ptr(x2), _ACT_CODES[x.dtype], m, k, n, _ptr(w), _ptr(s), _ptr(b), bcode,
-                                    _ptr(y), None, 0, _stream(x))
-    _lib.check(rc, "nsq_fp8_linear")
-    return y.reshape(*lead, n)
+    y = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    if bias is None:
+        bptr, bcode = None, _lib.DTYPE_NONE
+    else:
+        b, bcode = _bias_arg(bias)
+        bptr = b.data_ptr()
+    s = weight_scale
+    if s.dtype != torch.float32 or s.numel() != 1 or not s.is_contiguous():
+        s = _scale_arg(s)
+    rc = _lib.load().nsq_fp8_linear(x2.data_ptr(), code, m, k, n, w.data_ptr(), s.data_ptr(), bptr, bcode,
+                                    y.data_ptr(), None, 0, _stream(x))
+    if rc:
+        _lib.check(rc, "nsq_fp8_linear")
+    return y if x.dim() == 2 else y.reshape(*x.shape[:-1], n)
 
 
 def fp8_dequant(weight_fp8: torch.Tensor, weight_scale: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
