@@ -36,6 +36,8 @@ JSON), for Nsight Compute captures of a small case (one kernel, <= 4 launches):
   down8192       FP8 down 4864->896 at M=8192 (the sweep's paired-kernel launch), 3 launches
   awq0           config-0 AWQ linear (M=16, K=896, N=9728), 4 launches
   awq_llama_gate / fp8_llama_gate   Llama-3-8B gate 4096->14336 at M=16, 3 launches
+  sweep_prefill / sweep_decode      the sweep's M > 64 (M <= 64) FP8 linears once each,
+                 for a per-launch DRAM traffic table (metrics of one pass only)
 """
 
 from __future__ import annotations
@@ -860,6 +862,12 @@ def run_ncu_case(name):
             codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
             for _ in range(3):
                 ops.fp8_linear(x, codes, scale)
+    elif name in ("sweep_prefill", "sweep_decode"):
+        for _, k, n in SHAPES:
+            codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
+            for m in [mm for mm in MS if (mm <= 64) == (name == "sweep_decode")]:
+                x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+                ops.fp8_linear(x, codes, scale)
     elif name == "awq0":
         m, k, n, gs = 16, 896, 9728, 128
         for _ in range(4):
@@ -890,7 +898,8 @@ def main():
     ap.add_argument("--tp-overlap", type=int, default=0, metavar="TOKENS",
                     help="row-parallel layers overlap chunked GEMMs with their all-reduces from this many tokens "
                          "(0: off, the default)")
-    ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0", "awq_llama_gate", "fp8_llama_gate"],
+    ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0", "awq_llama_gate", "fp8_llama_gate",
+                                           "sweep_prefill", "sweep_decode"],
                     default=None,
                     help="run a small case of one kernel class for a profiler capture, then exit")
     args = ap.parse_args()

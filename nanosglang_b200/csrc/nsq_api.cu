@@ -105,12 +105,13 @@ namespace {
 // call. The key is every input of the encoding, so a hit is exactly what the
 // driver would return.
 struct MapKey {
-  uint64_t base, inner, outer, stride;
-  uint32_t box_inner, box_outer;
-  int dtype, swizzle;
+  uint64_t base, dim[3], stride[2];
+  uint32_t box[3];
+  int rank, dtype, swizzle;
   bool operator==(const MapKey& o) const {
-    return base == o.base && inner == o.inner && outer == o.outer && stride == o.stride &&
-           box_inner == o.box_inner && box_outer == o.box_outer && dtype == o.dtype && swizzle == o.swizzle;
+    return base == o.base && dim[0] == o.dim[0] && dim[1] == o.dim[1] && dim[2] == o.dim[2] &&
+           stride[0] == o.stride[0] && stride[1] == o.stride[1] && box[0] == o.box[0] && box[1] == o.box[1] &&
+           box[2] == o.box[2] && rank == o.rank && dtype == o.dtype && swizzle == o.swizzle;
   }
 };
 struct MapEntry {
@@ -122,19 +123,20 @@ constexpr int kMapCache = 64;
 thread_local MapEntry t_map_cache[kMapCache];
 
 inline uint32_t map_slot(const MapKey& k) {
-  uint64_t h = k.base * 0x9E3779B97F4A7C15ull ^ (k.inner * 0xC2B2AE3D27D4EB4Full) ^ (k.outer << 17) ^
-               (k.stride << 7) ^ ((uint64_t)k.box_inner << 40) ^ ((uint64_t)k.box_outer << 24) ^
-               ((uint64_t)k.dtype << 56) ^ ((uint64_t)k.swizzle << 60);
+  uint64_t h = k.base * 0x9E3779B97F4A7C15ull ^ (k.dim[0] * 0xC2B2AE3D27D4EB4Full) ^ (k.dim[1] << 17) ^
+               (k.dim[2] << 33) ^ (k.stride[0] << 7) ^ (k.stride[1] << 21) ^ ((uint64_t)k.box[0] << 40) ^
+               ((uint64_t)k.box[1] << 24) ^ ((uint64_t)k.box[2] << 48) ^ ((uint64_t)k.dtype << 56) ^
+               ((uint64_t)k.swizzle << 60) ^ ((uint64_t)k.rank << 62);
   h ^= h >> 29;
   return (uint32_t)(h % kMapCache);
 }
 }  // namespace
 
-CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
-                              uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                              uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
-  const MapKey key{reinterpret_cast<uint64_t>(base), inner, outer, row_stride_bytes, box_inner, box_outer,
-                   (int)dtype, (int)swizzle};
+static CUresult encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, void* base, int rank,
+                                  const uint64_t (&dim)[3], const uint64_t (&stride)[2], const uint32_t (&boxd)[3],
+                                  CUtensorMapSwizzle swizzle) {
+  const MapKey key{reinterpret_cast<uint64_t>(base), {dim[0], dim[1], dim[2]}, {stride[0], stride[1]},
+                   {boxd[0], boxd[1], boxd[2]}, rank, (int)dtype, (int)swizzle};
   MapEntry& slot = t_map_cache[map_slot(key)];
   if (slot.valid && slot.key == key) {
     *map = slot.map;
@@ -156,18 +158,31 @@ CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void*
       g_encode.store(encode, std::memory_order_release);
     }
   }
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {row_stride_bytes};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(map, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const cuuint64_t dims[3] = {dim[0], dim[1], dim[2]};
+  const cuuint64_t strides[2] = {stride[0], stride[1]};
+  const cuuint32_t box[3] = {boxd[0], boxd[1], boxd[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, dtype, (cuuint32_t)rank, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r == CUDA_SUCCESS) {
     slot.key = key;
     slot.map = *map;
     slot.valid = true;
   }
   return r;
+}
+
+CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
+                              uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                              uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  return encode_tensor_map(map, dtype, base, 2, {inner, outer, 0}, {row_stride_bytes, 0}, {box_inner, box_outer, 0},
+                           swizzle);
+}
+
+CUresult encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, void* base, uint64_t d0, uint64_t d1,
+                              uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                              uint32_t b2, CUtensorMapSwizzle swizzle) {
+  return encode_tensor_map(map, dtype, base, 3, {d0, d1, d2}, {stride1_bytes, stride2_bytes}, {b0, b1, b2}, swizzle);
 }
 
 }  // namespace nsq
@@ -277,7 +292,19 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     // and the Qwen2.5-0.5B shapes stay on the kernels below). AWQ group sizes
     // 32 and 64 run here for every M <= 32.
     const bool small_group = a.fmt == 0 && a.group_size % 128 != 0;
-    if (a.M <= 32 && (small_group || ((int64_t)a.K * a.N >= ((int64_t)1 << 24) && (a.fmt == 1 || a.M > 16)))) {
+    // Layers of 64-128 rows per SM: the tensor-core decode kernel (the UMMA
+    // reads the stored weight; x as two narrow terms) for FP8 at 2..32 tokens
+    // and AWQ at 17..32 tokens or on weights of 64 M+ elements (B200, CUDA-graph
+    // chains: FP8 4096 -> 14336 at M = 16 23.3 -> 21.3 us, M = 32 29.3 -> 24.4
+    // us; AWQ 8192 -> 18944 at M = 16 107 -> 56 us, 4096 -> 14336 at M = 32
+    // 37.2 -> 35.5 us; AWQ at M <= 16 on smaller weights stays on the
+    // weight-ring kernel, 23.9 vs 27.8 us)
+    if (a.M <= 32 && !small_group && decode_tc_rows(a) > 0 &&
+        (a.fmt == 1 ? a.M >= 2 : (a.M > 16 || (int64_t)a.K * a.N >= ((int64_t)1 << 26)))) {
+      const int rc = run_decode_tc_linear(a, stream);
+      if (rc != NSQ_ENOTSUP) return rc;
+    }
+    if (a.M <= 32 && (small_group ||((int64_t)a.K * a.N >= ((int64_t)1 << 24) && (a.fmt == 1 || a.M > 16)))) {
       const int rc = run_decode_rows_linear(a, stream);
       if (rc != NSQ_ENOTSUP || small_group) return rc;
     }

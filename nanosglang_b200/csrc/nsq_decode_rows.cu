@@ -515,6 +515,8 @@ __global__ void __launch_bounds__(kThreadsRows, 1) decode_rows_kernel(const __gr
       }
     }
     // the stage's smem may be refilled once every consumer warp is done with it
+    // (FP8: this thread's in-place x stores precede the next copy into the slot)
+    if constexpr (FMT == 1 && BF16) fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }

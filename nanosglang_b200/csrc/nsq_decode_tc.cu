@@ -1,0 +1,681 @@
+// Tensor-core decode linear (M <= 32 tokens) for layers of at least 64 rows per
+// SM: the tcgen05 UMMAs read the weight straight from the TMA-staged tiles, and
+// x enters the tensor core as two narrow terms, so no CUDA-core instruction
+// touches the weight values (FP8) or only widens nibbles to bytes (AWQ).
+//
+// Replaces AWQLinear.forward / FP8Linear.forward (nano_sglang/decode/
+// quantization.py:150-152 and :49-52) for small batches on large layers
+// (Llama-3-8B / Qwen2.5-72B gate, up, fused q/k/v). The reference dequantises
+// the weight and calls cuBLAS.
+//
+// Why: the warp-MMA decode kernels spend their time converting weights on the
+// CUDA cores (one conversion per two e4m3 codes on a 16-lane pipe; a lop3 and
+// a subtract per two nibbles plus operand shuffles), and on B200 that, not
+// HBM, set their pace on large layers. Here the tensor core takes the weight
+// in its stored type:
+//   FP8: kind::f8f6f4, A = e4m3 codes as stored, B = x as two e4m3 terms;
+//   AWQ: kind::i8, A = nibbles widened to u8 (0..15, one lop3 per four), B = x
+//        as two s8 terms; zero point and group scale applied per 128-column
+//        k-block in the epilogue: s * (sum q x - z * sum x).
+// x terms, per token and k-block of 128 columns (one power-of-two scale 2^e):
+//   AWQ: x * 2^-e = T1 + T2 / 128, T1, T2 integers in [-64, 64] (max |x| of the
+//        block maps into [32, 64)): 13 bits of the block's range, so every
+//        element within 2^-4 of the block's largest keeps its bf16 precision;
+//   FP8: x * 2^-e = T1 + T2 / 16, T1 = e4m3(x * 2^-e), T2 = e4m3 of the
+//        remainder times 16 (max |x| maps into [128, 256)): about 8 significant
+//        bits per element, an element's own bf16 precision, down to 2^-14 of
+//        the block's largest.
+// Integer products (AWQ) are exact; the accumulators are fp32 throughout.
+//
+// Work split: CTA i owns weight rows [i R, i R + R), R <= 128 (one TMA box per
+// k-block, TMEM lane = row), and the whole K range; no split-K, no workspace.
+// Warp roles (AWQ 576 threads, FP8 448):
+//   warp 0      TMA producer (one lane): k-blocks of the weight rows, straight
+//               into the UMMA A ring (FP8), or pairs of k-blocks of packed
+//               nibbles into a raw ring (AWQ). Weights are static, so it never
+//               waits for the previous kernel.
+//   warp 1      TMEM owner and UMMA issuer: per k-block four UMMAs (M = 128,
+//               N = 2 MP, K = 32) into one of four accumulators, then commits
+//               that free the A block, the x-term tile and fill the accumulator.
+//   warps 2-9   x terms, two groups of four warps taking alternate k-blocks:
+//               x k-blocks by TMA, four ahead; per k-block and token the scale
+//               2^e, T1 and T2 in the UMMA B layout (K-major, 128-byte
+//               swizzle), and the per-token sums of the terms (AWQ zero point).
+//   warps 10-13 epilogue: warp w reads TMEM sub-partition w % 4 (32 rows)
+//               after every k-block and accumulates in registers.
+//   warps 14-17 (AWQ) nibble widening: raw ring -> A ring.
+// Every wait is bounded.
+#include <atomic>
+
+#include "nsq_common.cuh"
+#include "nsq_internal.h"
+
+namespace nsq {
+
+namespace {
+
+constexpr int kTcM = 128;                  // UMMA M: weight rows per CTA tile (TMEM lanes)
+constexpr int kTcWarpProd = 0;
+constexpr int kTcWarpMma = 1;
+constexpr int kTcWarpPrep0 = 2;
+constexpr int kTcPrepWarps = 8;
+constexpr int kTcXGroups = 2;  // x-term groups of four warps, alternating k-blocks
+constexpr int kTcWarpEpi0 = kTcWarpPrep0 + kTcPrepWarps;
+constexpr int kTcEpiWarps = 4;
+constexpr int kTcWarpUnp0 = kTcWarpEpi0 + kTcEpiWarps;
+constexpr int kTcUnpWarps = 4;
+constexpr int kTcND = 4;   // accumulators in TMEM
+constexpr int kTcNB = 4;   // x-term tiles
+constexpr int kTcNX = 8;   // per-token scalars of a k-block
+constexpr int kTcNXR = 4;  // x k-blocks staged ahead of the x-term warps
+constexpr uint32_t kTcTmemCols = 256;
+
+constexpr int kTcMaxNS = 12;  // weight stages (upper bound; the plan sizes the ring to shared memory)
+constexpr int kTcMaxNA = 4;  // widened k-block tiles (AWQ)
+constexpr int kTcSmemMax = 227 * 1024;
+
+// FP8: the weight ring holds the UMMA A tiles themselves (one 128-byte box of
+// every row per k-block, straight from TMA); AWQ: the ring holds raw tiles of
+// packed nibbles (128 bytes of every row = two k-blocks), widened into A tiles.
+template <int FMT>
+struct TcCfg {
+  static constexpr int kThreads = (FMT == 0 ? kTcWarpUnp0 + kTcUnpWarps : kTcWarpUnp0) * 32;
+  static constexpr int kKPS = FMT == 0 ? 2 : 1;  // k-blocks per ring slot
+};
+
+// Fixed part of the shared-memory layout (after the weight rings, whose size
+// the plan chooses): x-term tiles, x k-blocks, per-token scalars, barriers.
+template <int MP>
+struct TcFixed {
+  static constexpr int kBBytes = 2 * MP * 128;  // x-term tile: 2 MP rows (T1 rows, then T2 rows) x 128 B
+  static constexpr int kXBytes = MP * 256;      // one x k-block: two boxes of [MP tokens x 64 columns] 16-bit
+  static constexpr int kB = 0;
+  static constexpr int kX = kB + kTcNB * kBBytes;
+  static constexpr int kXs = kX + kTcNXR * kXBytes;  // [NX][2][MP] fp32: scale 2^e, term sum (AWQ)
+  static constexpr int kBar = kXs + kTcNX * 2 * MP * 4;
+  static constexpr int kNumBars = 2 * kTcMaxNS + 2 * kTcMaxNA + 2 * kTcNB + 2 * kTcND + 2 * kTcNX + kTcNXR + 1;
+  static constexpr int kTmemSlot = kBar + kNumBars * 8;
+  static constexpr int kAbort = kTmemSlot + 4;
+  static constexpr int kBytes = ((kAbort + 4 + 1023) / 1024) * 1024;
+  static_assert(kBBytes % 1024 == 0 && kXBytes % 1024 == 0, "tiles stay 1 KB aligned");
+  static_assert(kTcNB * kBBytes >= 16 * 1024, "the last UMMA A tile may read up to 16 KB past its start");
+};
+
+struct TcParams {
+  const void* x;
+  const __half* scales;  // AWQ [N, G]
+  const __half* zeros;   // AWQ [N, G]
+  const float* wscale;   // FP8 per-tensor scale (device)
+  const void* bias;
+  void* y;
+  DevStatus* status;
+  int M, K, N;
+  int G, group_size;
+  int bias_dtype;
+  int rlo, nhi;  // weight rows per CTA: rlo + 8 for the first nhi CTAs, rlo for the others (multiples of 8)
+  int nkb;       // k-blocks of 128 columns
+  int tile;      // bytes of one k-block tile of the tallest CTA: (rlo + 8) x 128 B
+  int ns;    // weight stages in the ring
+  int na;    // A tiles
+  int off_raw, off_fixed;  // weight ring; fixed part (TcFixed)
+};
+
+// Instruction descriptor: AWQ kind::i8 (A u8, B s8, D s32), FP8 kind::f8f6f4
+// (A, B e4m3, D f32); both operands K-major.
+__host__ __device__ constexpr uint32_t tc_idesc(int fmt, int m, int n) {
+  return (fmt == 0 ? ((2u << 4) | (0u << 7) | (1u << 10)) : ((1u << 4) | (0u << 7) | (0u << 10))) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// The four UMMAs of one k-block (K = 32 each: 32 bytes of every 128-byte row
+// per step, +2 in descriptor units), issued by the elected lane of a converged
+// warp in one asm block; the first starts a fresh accumulator.
+template <int FMT>
+__device__ __forceinline__ void tc_umma_k128_elect(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc) {
+#define NSQ_TC_UMMA(KIND)                                                                        \
+  asm volatile(                                                                                  \
+      "{\n\t.reg .pred e, p, t;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"              \
+      "setp.ne.b32 p, %9, %9;\n\tsetp.eq.b32 t, %9, %9;\n\t"                                     \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %1, %5, %9, p;\n\t"                     \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %2, %6, %9, t;\n\t"                     \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %3, %7, %9, t;\n\t"                     \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %4, %8, %9, t;\n\t}" ::"r"(d),          \
+      "l"(a), "l"(a + 2), "l"(a + 4), "l"(a + 6), "l"(b), "l"(b + 2), "l"(b + 4), "l"(b + 6),  \
+      "r"(idesc)                                                                                 \
+      : "memory")
+  if constexpr (FMT == 0) {
+    NSQ_TC_UMMA("i8");
+  } else {
+    NSQ_TC_UMMA("f8f6f4");
+  }
+#undef NSQ_TC_UMMA
+}
+
+// One rank-3 TMA box into shared memory (no multicast), completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// bytes 0 of a, b, c, d -> one word (a in the low byte)
+__device__ __forceinline__ uint32_t pack_b0(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return prmt(prmt(a, b, 0x5140u), prmt(c, d, 0x5140u), 0x5410u);
+}
+
+// two floats -> two e4m3 codes (hi in the upper byte), round to nearest, saturating
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float hi, float lo) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// two e4m3 codes (low byte first) -> their two values
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t codes16) {
+  uint32_t h;
+  asm("{\n\t.reg .b16 c;\n\tcvt.u16.u32 c, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, c;\n\t}" : "=r"(h) : "r"(codes16));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+template <int FMT, bool BF16, int MP>
+__global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap wmap_lo,
+                                                                             const __grid_constant__ CUtensorMap wmap_hi,
+                                                                             const __grid_constant__ CUtensorMap xmap,
+                                                                             const TcParams p) {
+  using F = TcFixed<MP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* fx = smem + p.off_fixed;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fx + F::kBar);
+  // Weight ring (one box of 128 bytes of every row per slot, filled by TMA):
+  // wfull / wempty. AWQ A tiles (one k-block each, widened from the ring):
+  // afull / aempty (their UMMAs finished). bfull / bempty:
+  // x-term tiles. dfull: an accumulator's UMMAs finished; dempty: its four
+  // readers are done. xsfull / xsempty: the per-token scalars of a k-block.
+  // Tiles are `tile` bytes apart (rows rounded up to 8): a UMMA reads 128 rows
+  // from a tile's start, so the rows past this CTA's come from the next tile
+  // (their accumulator lanes are never read).
+  uint64_t* wfull = bars;
+  uint64_t* wempty = wfull + kTcMaxNS;
+  uint64_t* afull = wempty + kTcMaxNS;
+  uint64_t* aempty = afull + kTcMaxNA;
+  uint64_t* bfull = aempty + kTcMaxNA;
+  uint64_t* bempty = bfull + kTcNB;
+  uint64_t* dfull = bempty + kTcNB;
+  uint64_t* dempty = dfull + kTcND;
+  uint64_t* xsfull = dempty + kTcND;
+  uint64_t* xsempty = xsfull + kTcNX;
+  uint64_t* xfull = xsempty + kTcNX;
+  uint64_t* mdone = xfull + kTcNXR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fx + F::kTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(fx + F::kAbort);
+  float* xs = reinterpret_cast<float*>(fx + F::kXs);
+  constexpr int KPS = TcCfg<FMT>::kKPS;
+  const int NS = p.ns, NA = p.na;
+  const uint32_t tile = (uint32_t)p.tile;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i_cta = (int)blockIdx.x;
+  const int rows = i_cta < p.nhi ? p.rlo + 8 : p.rlo;      // this CTA's rows (multiple of 8)
+  const int r0 = i_cta * p.rlo + 8 * min(i_cta, p.nhi);
+  const int rvalid = min(rows, p.N - r0);
+  const CUtensorMap* wmap = i_cta < p.nhi ? &wmap_hi : &wmap_lo;
+  const uint32_t ctile = (uint32_t)rows * 128u;  // k-block tile pitch inside a weight stage
+  const int nkb = p.nkb;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&wfull[i], 1);
+      mbar_init(&wempty[i], FMT == 0 ? kTcUnpWarps : 1);
+    }
+    for (int i = 0; i < NA; ++i) {
+      mbar_init(&afull[i], kTcUnpWarps);
+      mbar_init(&aempty[i], 1);
+    }
+    for (int i = 0; i < kTcNB; ++i) {
+      mbar_init(&bfull[i], 1);
+      mbar_init(&bempty[i], 1);
+    }
+    for (int i = 0; i < kTcND; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], 4);
+    }
+    for (int i = 0; i < kTcNX; ++i) {
+      mbar_init(&xsfull[i], 1);
+      mbar_init(&xsempty[i], 4);
+    }
+    for (int i = 0; i < kTcNXR; ++i) mbar_init(&xfull[i], 1);
+    mbar_init(mdone, 1);
+    fence_barrier_init();
+  }
+  if (warp == kTcWarpMma) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  bool ok = true;
+
+  if (warp == kTcWarpProd) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      // Slot st: the box [rows][128 B] of 128-byte chunk st of every row (one
+      // FP8 k-block, or two AWQ k-blocks of packed nibbles). Chunks past the
+      // row read zeros; their k-blocks are never used.
+      tma_prefetch_desc(wmap);
+      const int nst = (nkb + KPS - 1) / KPS;
+      uint8_t* ring = smem + p.off_raw;
+      int st = 0;
+      for (; st < nst; ++st) {
+        const int slot = st % NS;
+        if (st >= NS && !(ok = mbar_wait(&wempty[slot], ((st / NS) - 1) & 1, p.status, 80, abort_flag))) break;
+        mbar_arrive_expect_tx(&wfull[slot], ctile);
+        tma_load_2d(ring + (size_t)slot * tile, wmap, &wfull[slot], st * 32, r0);
+      }
+      if (!ok) {  // copies in flight land before the CTA can exit
+        for (int j = (st > NS ? st - NS : 0); j < st; ++j) mbar_wait(&wfull[j % NS], (j / NS) & 1, nullptr, 0, nullptr);
+      }
+    }
+  } else if (warp == kTcWarpMma) {
+    // ---------------- UMMA issuer (whole warp, converged) ----------------
+    const uint32_t idesc = tc_idesc(FMT, kTcM, 2 * MP);
+    for (int b = 0; b < nkb; ++b) {
+      const int s = b % kTcNB, d = b % kTcND;
+      // the A tile of k-block b: FP8 ring slot b % ns; AWQ widened tile b % na
+      const int a = FMT == 1 ? b % NS : b % NA;
+      if constexpr (FMT == 1) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&wfull[a], (b / NS) & 1, p.status, 81, abort_flag));
+      } else {
+        ok = __all_sync(0xffffffffu, mbar_wait(&afull[a], (b / NA) & 1, p.status, 82, abort_flag));
+      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bfull[s], (b / kTcNB) & 1, p.status, 83, abort_flag));
+      if (ok && b >= kTcND) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&dempty[d], ((b / kTcND) - 1) & 1, p.status, 84, abort_flag));
+      }
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t adesc = sw128_kmajor_desc(smem_u32(smem + (FMT == 1 ? p.off_raw : 0)) + (uint32_t)a * tile);
+      const uint64_t bdesc = sw128_kmajor_desc(smem_u32(fx + F::kB + s * F::kBBytes));
+      tc_umma_k128_elect<FMT>(tmem_base + (uint32_t)(d * 2 * MP), adesc, bdesc, idesc);
+      tc_commit_elect(FMT == 1 ? &wempty[a] : &aempty[a]);
+      tc_commit_elect(&bempty[s]);
+      tc_commit_elect(&dfull[d]);
+    }
+    // every UMMA issued has finished before TMEM is released
+    tc_commit_elect(mdone);
+    mbar_wait(mdone, 0, nullptr, 0, nullptr);
+  } else if (warp < kTcWarpEpi0) {
+    // ---------------- x terms ----------------
+    pdl_wait_prior_grids();  // x is written by the previous kernel
+    constexpr int kGT = kTcPrepWarps / kTcXGroups * 32;  // threads of a group
+    constexpr int TPT = kGT / MP;                        // threads per token
+    constexpr int EPT = 128 / TPT;                       // columns per thread: one or two 16-byte chunks of a term row
+    static_assert(EPT == 16 || EPT == 32, "16 or 32 token slots");
+    static_assert(kTcNXR % kTcXGroups == 0 && kTcNB % kTcXGroups == 0 && kTcNX % kTcXGroups == 0, "group slots");
+    const int grp = (threadIdx.x - kTcWarpPrep0 * 32) / kGT;  // this group takes k-blocks grp, grp + 2, ...
+    const int t = threadIdx.x - kTcWarpPrep0 * 32 - grp * kGT;
+    const int tok = t / TPT, part = t - (t / TPT) * TPT;
+    // x k-blocks arrive by TMA, kTcNXR ahead: [2 boxes][MP tokens][64 columns]
+    // (tokens past M are zero-filled)
+    int xissued = 0;
+    auto issue_x = [&](int b) {
+      const int slot = b % kTcNXR;
+      mbar_arrive_expect_tx(&xfull[slot], (uint32_t)F::kXBytes);
+      tma_load_3d(fx + F::kX + slot * F::kXBytes, &xmap, &xfull[slot], 0, 0, b * 2);
+      ++xissued;
+    };
+    if (t == 0) {
+      tma_prefetch_desc(&xmap);
+      for (int b = grp; b < nkb && b < kTcNXR; b += kTcXGroups) issue_x(b);
+    }
+    const int xc0 = part * EPT;  // first column of this thread within the k-block
+    const uint32_t xsrc0 = (uint32_t)((xc0 >> 6) * (F::kXBytes / 2) + tok * 128 + (xc0 & 63) * 2);
+    for (int b = grp; b < nkb; b += kTcXGroups) {
+      const int s = b % kTcNB, xsl = b % kTcNX, xr = b % kTcNXR;
+      if (b >= kTcNB && !(ok = mbar_wait(&bempty[s], ((b / kTcNB) - 1) & 1, p.status, 85, abort_flag))) break;
+      if (b >= kTcNX && !(ok = mbar_wait(&xsempty[xsl], ((b / kTcNX) - 1) & 1, p.status, 86, abort_flag))) break;
+      if (!(ok = mbar_wait(&xfull[xr], (b / kTcNXR) & 1, p.status, 91, abort_flag))) break;
+      const uint32_t xsrc = smem_u32(fx + F::kX + xr * F::kXBytes) + xsrc0;
+      uint4 v[EPT / 8];
+#pragma unroll
+      for (int i = 0; i < EPT / 8; ++i) v[i] = lds128(xsrc + 16 * i);
+      float f[EPT];
+#pragma unroll
+      for (int i = 0; i < EPT / 8; ++i) {
+        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          f[8 * i + 2 * e] = elem_to_float<BF16>((uint16_t)(w[e] & 0xFFFFu));
+          f[8 * i + 2 * e + 1] = elem_to_float<BF16>((uint16_t)(w[e] >> 16));
+        }
+      }
+      float mx = 0.f;
+#pragma unroll
+      for (int i = 0; i < EPT; ++i) mx = fmaxf(mx, fabsf(f[i]));
+#pragma unroll
+      for (int m = 1; m < TPT; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+      const int E = (__float_as_int(mx) >> 23) & 0xFF;  // biased exponent of the block's largest |x|
+      uint32_t o1[EPT / 4], o2[EPT / 4];                 // term bytes, in the A operand's column order
+      float sc = 0.f, sx = 0.f;
+      if constexpr (FMT == 0) {
+        // x * 2^-e in [-64, 64): e = E - 127 - 5; blocks below 2^-119 count as zero
+        const bool nz = E >= 12;
+        const float inv = nz ? __int_as_float((259 - E) << 23) : 0.f;
+        sc = nz ? __int_as_float((E - 5) << 23) : 0.f;
+        constexpr float kRnd = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer, kept in the low bits
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int g = 0; g < EPT / 8; ++g) {
+          uint32_t b1[8], b2[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float a1 = fmaf(f[8 * g + i], inv, kRnd);
+            const float t1 = a1 - kRnd;
+            const float rr = fmaf(f[8 * g + i], inv, -t1);
+            const float a2 = fmaf(rr, 128.0f, kRnd);
+            s1 += t1;
+            s2 += a2 - kRnd;
+            b1[i] = __float_as_uint(a1);  // low byte: the integer, two's complement
+            b2[i] = __float_as_uint(a2);
+          }
+          // widened weight bytes of one 32-bit word: columns 0,2,4,6 then 1,3,5,7
+          o1[2 * g] = pack_b0(b1[0], b1[2], b1[4], b1[6]);
+          o1[2 * g + 1] = pack_b0(b1[1], b1[3], b1[5], b1[7]);
+          o2[2 * g] = pack_b0(b2[0], b2[2], b2[4], b2[6]);
+          o2[2 * g + 1] = pack_b0(b2[1], b2[3], b2[5], b2[7]);
+        }
+#pragma unroll
+        for (int m = 1; m < TPT; m <<= 1) {
+          s1 += __shfl_xor_sync(0xffffffffu, s1, m);
+          s2 += __shfl_xor_sync(0xffffffffu, s2, m);
+        }
+        sx = s1 + s2 * 0.0078125f;
+      } else {
+        // x * 2^-e with its largest in [128, 256): e = E - 127 - 7; blocks below 2^-115 count as zero
+        const bool nz = E >= 12;
+        const float inv = nz ? __int_as_float((261 - E) << 23) : 0.f;
+        sc = nz ? __int_as_float((E - 7) << 23) : 0.f;
+#pragma unroll
+        for (int i = 0; i < EPT; i += 4) {
+          const float x0 = f[i] * inv, x1 = f[i + 1] * inv, x2 = f[i + 2] * inv, x3 = f[i + 3] * inv;
+          const uint32_t c01 = f32x2_to_e4m3x2(x1, x0), c23 = f32x2_to_e4m3x2(x3, x2);
+          const float2 v01 = e4m3x2_to_f32x2(c01), v23 = e4m3x2_to_f32x2(c23);
+          const uint32_t d01 = f32x2_to_e4m3x2((x1 - v01.y) * 16.0f, (x0 - v01.x) * 16.0f);
+          const uint32_t d23 = f32x2_to_e4m3x2((x3 - v23.y) * 16.0f, (x2 - v23.x) * 16.0f);
+          o1[i / 4] = c01 | (c23 << 16);
+          o2[i / 4] = d01 | (d23 << 16);
+        }
+      }
+      // term rows tok (T1) and MP + tok (T2) of the x-term tile
+      const uint32_t bt = smem_u32(fx + F::kB + s * F::kBBytes);
+#pragma unroll
+      for (int cc = 0; cc < EPT / 16; ++cc) {
+        const int chunk = part * (EPT / 16) + cc;
+        const int ra = tok, rb = MP + tok;
+        sts128(bt + ra * 128 + ((chunk ^ (ra & 7)) << 4), o1[4 * cc], o1[4 * cc + 1], o1[4 * cc + 2], o1[4 * cc + 3]);
+        sts128(bt + rb * 128 + ((chunk ^ (rb & 7)) << 4), o2[4 * cc], o2[4 * cc + 1], o2[4 * cc + 2], o2[4 * cc + 3]);
+      }
+      if (part == 0) {
+        xs[(xsl * 2) * MP + tok] = sc;
+        xs[(xsl * 2 + 1) * MP + tok] = sx;
+      }
+      // one proxy fence orders this thread's x reads before the slot's next
+      // copy and its term stores before the UMMAs that read them
+      fence_proxy_async_smem();
+      named_bar_sync(5 + grp, kGT);
+      if (t == 0) {
+        mbar_arrive(&bfull[s]);
+        mbar_arrive(&xsfull[xsl]);
+        if (b + kTcNXR < nkb) issue_x(b + kTcNXR);
+      }
+    }
+    if (t == 0 && !ok) {
+      // x copies in flight land before the CTA can exit: this group's i-th
+      // copy is of k-block grp + i * kTcXGroups; the last kTcNXR / kTcXGroups
+      // may not have been waited for
+      for (int i = xissued - kTcNXR / kTcXGroups; i < xissued; ++i) {
+        if (i < 0) continue;
+        const int bb = grp + i * kTcXGroups;
+        mbar_wait(&xfull[bb % kTcNXR], (bb / kTcNXR) & 1, nullptr, 0, nullptr);
+      }
+    }
+  } else if (warp < kTcWarpUnp0) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM sub-partition: rows 32 q .. 32 q + 31
+    const int row = q * 32 + lane;
+    const bool rv = row < rvalid;
+    const int n = r0 + row;
+    const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16);
+    float acc[MP];
+#pragma unroll
+    for (int i = 0; i < MP; ++i) acc[i] = 0.f;
+    const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
+    const unsigned short* zr16 = reinterpret_cast<const unsigned short*>(p.zeros);
+    // AWQ: (scale, zero point) of this row for the next k-block, loaded one block ahead
+    auto load_sz = [&](int b) -> uint32_t {
+      if (FMT != 0 || !rv || b >= nkb) return 0u;
+      const int64_t off = (int64_t)n * p.G + (b * 128) / p.group_size;
+      return (uint32_t)__ldg(sc16 + off) | ((uint32_t)__ldg(zr16 + off) << 16);
+    };
+    uint32_t sz_next = load_sz(0);
+    for (int b = 0; b < nkb; ++b) {
+      const int d = b % kTcND, xsl = b % kTcNX;
+      const uint32_t sz = sz_next;
+      sz_next = load_sz(b + 1);
+      if (!(ok = mbar_wait(&dfull[d], (b / kTcND) & 1, p.status, 87, abort_flag))) break;
+      if (!(ok = mbar_wait(&xsfull[xsl], (b / kTcNX) & 1, p.status, 88, abort_flag))) break;
+      tc_fence_after();
+      const float s = __half2float(__ushort_as_half((unsigned short)(sz & 0xFFFFu)));
+      const float z = __half2float(__ushort_as_half((unsigned short)(sz >> 16)));
+      const float* xsc = xs + (xsl * 2) * MP;
+      const float* xsx = xs + (xsl * 2 + 1) * MP;
+#pragma unroll
+      for (int th = 0; th < MP; th += 16) {
+        uint32_t ra[16], rb[16];
+        tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + th), ra);
+        tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + MP + th), rb);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float scl = xsc[th + i];
+          if constexpr (FMT == 0) {
+            const float v = (float)((int)ra[i] * 128 + (int)rb[i]);
+            acc[th + i] = fmaf(s * scl, fmaf(v, 0.0078125f, -z * xsx[th + i]), acc[th + i]);
+          } else {
+            acc[th + i] = fmaf(__uint_as_float(ra[i]), scl, fmaf(__uint_as_float(rb[i]), scl * 0.0625f, acc[th + i]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&dempty[d]);
+        mbar_arrive(&xsempty[xsl]);
+      }
+    }
+    if (rv && ok) {
+      const float ws = (FMT == 1) ? __ldg(p.wscale) : 1.0f;
+      const float bn = p.bias_dtype != NSQ_DTYPE_NONE ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
+      uint16_t* y = static_cast<uint16_t*>(p.y);
+#pragma unroll
+      for (int i = 0; i < MP; ++i) {
+        if (i < p.M) {
+          const float v = acc[i] * ws + bn;
+          y[(int64_t)i * p.N + n] = float_to_elem<BF16>(v);
+        }
+      }
+    }
+  } else if constexpr (FMT == 0) {
+    // ---------------- nibble widening (AWQ) ----------------
+    // k-block h of a raw slot = 16-byte pieces 4h .. 4h + 3 of each 128-byte
+    // row; piece rc (32 columns, 4 words) becomes pieces 2 rc, 2 rc + 1 of
+    // the A tile: per word, the bytes of nibbles 0,2,4,6 then 1,3,5,7.
+    const int t = threadIdx.x - kTcWarpUnp0 * 32;
+    const int nst = (nkb + KPS - 1) / KPS;
+    const int items = rows * 4;
+    for (int st = 0; st < nst && ok; ++st) {
+      const int rs = st % NS;
+      if (!(ok = mbar_wait(&wfull[rs], (st / NS) & 1, p.status, 89, abort_flag))) break;
+      const uint32_t raw = smem_u32(smem + p.off_raw) + (uint32_t)rs * tile;
+      for (int h = 0; h < KPS; ++h) {
+        const int b = KPS * st + h;
+        if (b >= nkb) break;
+        const int a = b % NA;
+        if (b >= NA && !(ok = mbar_wait(&aempty[a], ((b / NA) - 1) & 1, p.status, 90, abort_flag))) break;
+        const uint32_t dst = smem_u32(smem) + (uint32_t)a * tile;
+        for (int i = t; i < items; i += kTcUnpWarps * 32) {
+          const int r = i >> 2, rc = i & 3;
+          const uint32_t rowb = (uint32_t)r * 128u;
+          const uint4 w = lds128(raw + rowb + (((h * 4 + rc) ^ (r & 7)) << 4));
+          sts128(dst + rowb + (((2 * rc) ^ (r & 7)) << 4), w.x & 0x0F0F0F0Fu, (w.x >> 4) & 0x0F0F0F0Fu,
+                 w.y & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu);
+          sts128(dst + rowb + (((2 * rc + 1) ^ (r & 7)) << 4), w.z & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                 w.w & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+        }
+        fence_proxy_async_smem();  // the tile is read by the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[a]);
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[rs]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == kTcWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTcTmemCols);
+  }
+}
+
+template <int FMT, bool BF16, int MP>
+cudaError_t launch_tc(const CUtensorMap& wlo, const CUtensorMap& whi, const CUtensorMap& xmap, const TcParams& p,
+                      int grid, cudaStream_t stream) {
+  auto kern = decode_tc_kernel<FMT, BF16, MP>;
+  static std::atomic<bool> configured{false};
+  if (!configured.load()) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
+    if (e != cudaSuccess) return e;
+    configured.store(true);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(TcCfg<FMT>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)p.off_fixed + TcFixed<MP>::kBytes + 1024;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    na = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, wlo, whi, xmap, p);
+}
+
+template <int FMT, bool BF16>
+cudaError_t dispatch_tc(int mp, const CUtensorMap& wlo, const CUtensorMap& whi, const CUtensorMap& xmap,
+                        const TcParams& p, int grid, cudaStream_t s) {
+  return mp == 16 ? launch_tc<FMT, BF16, 16>(wlo, whi, xmap, p, grid, s)
+                  : launch_tc<FMT, BF16, 32>(wlo, whi, xmap, p, grid, s);
+}
+
+}  // namespace
+
+namespace {
+// Rows per CTA in multiples of 8 (so every k-block tile of a stage stays on a
+// 1 KB swizzle boundary): rlo for most CTAs, rlo + 8 for the first nhi.
+bool tc_rows(const LinearArgs& a, int* rlo, int* nhi, int* grid) {
+  if (a.M < 1 || a.M > 32 || a.K % 128 != 0 || a.K < 256) return false;
+  if (a.fmt == 0 && (a.K % 256 != 0 || a.group_size % 128 != 0 || a.K % a.group_size != 0)) return false;
+  const int sms = num_sms();
+  const int g8 = (a.N + 7) / 8;
+  const int c = g8 < sms ? g8 : sms;
+  const int base = g8 / c, rem = g8 - base * c;
+  *rlo = 8 * base;
+  *nhi = rem;
+  *grid = c;
+  return *rlo >= 64 && *rlo + (rem > 0 ? 8 : 0) <= kTcM;
+}
+}  // namespace
+
+// Rows of the tallest CTA for the tensor-core decode kernel, 0 if it does not apply.
+int decode_tc_rows(const LinearArgs& a) {
+  int rlo, nhi, grid;
+  if (!tc_rows(a, &rlo, &nhi, &grid)) return 0;
+  return rlo + (nhi > 0 ? 8 : 0);
+}
+
+int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
+  int rlo, nhi, grid;
+  if (!tc_rows(a, &rlo, &nhi, &grid)) return NSQ_ENOTSUP;
+  const int rmax = rlo + (nhi > 0 ? 8 : 0);
+  const int mp = a.M <= 16 ? 16 : 32;
+  TcParams p{};
+  p.x = a.x;
+  p.scales = reinterpret_cast<const __half*>(a.scales);
+  p.zeros = reinterpret_cast<const __half*>(a.zeros);
+  p.wscale = a.wscale;
+  p.bias = a.bias;
+  p.y = a.y;
+  p.status = device_status_ptr();
+  p.M = a.M;
+  p.K = a.K;
+  p.N = a.N;
+  p.group_size = a.fmt == 0 ? a.group_size : 0;
+  p.G = a.fmt == 0 ? a.K / a.group_size : 0;
+  p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
+  p.rlo = rlo;
+  p.nhi = nhi;
+  p.nkb = a.K / 128;
+  // Shared memory: AWQ A tiles, the weight ring (sized to what is left, at
+  // most kTcMaxNS slots), the fixed part. A UMMA reads 128 rows from a tile's
+  // start, so the rows past this CTA's come from the next tile (their
+  // accumulator lanes are never read).
+  p.tile = rmax * 128;
+  const int fixed = mp == 16 ? TcFixed<16>::kBytes : TcFixed<32>::kBytes;
+  const int room = kTcSmemMax - 1024 - fixed;
+  p.na = a.fmt == 0 ? kTcMaxNA : 0;
+  p.ns = (room - p.na * p.tile) / p.tile;
+  if (p.ns > kTcMaxNS) p.ns = kTcMaxNS;
+  p.off_raw = p.na * p.tile;
+  p.off_fixed = p.off_raw + p.ns * p.tile;
+  if (p.ns < 4) return NSQ_ENOTSUP;
+  // weights as 32-bit words [N rows x K/8 (AWQ) or K/4 (FP8)], boxes of
+  // [rows of the CTA x 32 words = 128 B], 128-byte swizzle
+  const uint64_t row_bytes = a.fmt == 0 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
+  CUtensorMap wmap_lo, wmap_hi;
+  CUresult cr = encode_tensor_map_2d(&wmap_lo, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<void*>(a.wq), row_bytes / 4,
+                                     (uint64_t)a.N, row_bytes, 32, (uint32_t)rlo, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  cr = encode_tensor_map_2d(&wmap_hi, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<void*>(a.wq), row_bytes / 4,
+                            (uint64_t)a.N, row_bytes, 32, (uint32_t)rmax, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  // x, rank 3: [64-column halves of a k-block][tokens][64 columns] 16-bit, one
+  // box of [2][mp][64] per k-block (tokens past M read as zero)
+  CUtensorMap xmap;
+  cr = encode_tensor_map_3d(&xmap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            const_cast<void*>(a.x), 64, (uint64_t)a.M, (uint64_t)a.K / 64, (uint64_t)a.K * 2, 128, 64,
+                            (uint32_t)mp, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
+  cudaError_t e;
+  if (a.fmt == 0) {
+    e = a.x_bf16 ? dispatch_tc<0, true>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream)
+                 : dispatch_tc<0, false>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream);
+  } else {
+    e = a.x_bf16 ? dispatch_tc<1, true>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream)
+                 : dispatch_tc<1, false>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream);
+  }
+  return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
+}
+
+}  // namespace nsq

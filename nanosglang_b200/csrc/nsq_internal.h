@@ -21,6 +21,11 @@ bool test_withhold();  // failure-path test hook: the multi-wave decode kernel s
 CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
                               uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+// Rank 3: dims d0 (contiguous), d1, d2 with byte strides of d1 and d2; box b0 x b1 x b2
+// (shared memory gets the box with d0 fastest, then d1, then d2).
+CUresult encode_tensor_map_3d(CUtensorMap* map, CUtensorMapDataType dtype, void* base, uint64_t d0, uint64_t d1,
+                              uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1,
+                              uint32_t b2, CUtensorMapSwizzle swizzle);
 
 // elementwise
 cudaError_t launch_awq_dequant(const int32_t* qweight, const uint16_t* scales,
@@ -83,6 +88,10 @@ struct RowsLaunch {
 };
 int run_decode_rows(const RowsLaunch& L, cudaStream_t stream);
 int run_decode_rows_linear(const LinearArgs& a, cudaStream_t stream);
+// Tensor-core decode kernel (M <= 32, K % 128 == 0, AWQ groups of 128 k, 64 to
+// 128 weight rows per SM): rows per CTA, or 0 if it does not apply.
+int decode_tc_rows(const LinearArgs& a);
+int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream);
 // prefill: the weight tile dequantised into tensor memory (A operand), tokens
 // as UMMA N. One CTA per 128 weight rows x 64/128 tokens, K optionally split
 // over a cluster (small outputs, few-tile long-K layers), or CTA pairs with
