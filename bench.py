@@ -19,6 +19,9 @@ absmax/448 scale, bf16 N(0,1) activations. Random init, synthetic data.
   awq_config0  BASELINE config 0: AWQ W4A16 M=16, K=896, N=9728, cold-L2
            per-linear mean inside a CUDA graph over > 2x L2 of distinct
            weight copies; GB/s vs the measured HBM copy bandwidth.
+  decode_large  the same measurement on a large decode layer, Llama-3-8B
+           gate 4096 -> 14336 at M = 16 (FP8 and AWQ g128): the shapes where
+           the HBM roofline is reachable (59 / 31 MB per linear).
   parity   every one of the 42 outputs of the timed graph against an fp32
            product of the bit-exact dequantised weight (max relative
            Frobenius error; the bar is 1e-2). Under torchrun the sharded
@@ -483,8 +486,10 @@ def run_ours(args):
 
     # --- config 0: AWQ W4A16 decode linear, cold L2 -------------------------
     awq = None
+    dec_large = None
     if world == 1:
         awq = bench_awq_config0(torch, ops, device, args, peaks, peak_src, flush)
+        dec_large = bench_decode_large(torch, ops, device, args, peaks, peak_src, flush)
 
     # --- model level: configs 2 and 3 (tok/s) -------------------------------
     tok_s = None
@@ -509,7 +514,8 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": sweep_config(world),
-            "roofline": roofline, "decode_kernel": decode_line, "awq_config0": awq, "cpu_baseline": cpu,
+            "roofline": roofline, "decode_kernel": decode_line, "awq_config0": awq, "decode_large": dec_large,
+            "cpu_baseline": cpu,
             "e2e": e2e, "gpu_launches": len(cases) * args.steps, "clocks": clocks, "parity": parity,
             "tok_s": tok_s, "host_overhead": host,
         }
@@ -761,6 +767,72 @@ def bench_config3_tok_s(torch, dist, device, rank, world, args):
             "allreduce": ("one-shot NVLink peer all-reduce (nsq_peer_allreduce)" if peer else "NCCL")
             if world > 1 else None,
             "method": f"{steps} replays of the batch-64 decode-step graph, max over ranks"}
+
+
+def bench_decode_large(torch, ops, device, args, peaks, peak_src, flush):
+    """Llama-3-8B gate (K=4096 -> N=14336) at M=16, FP8 and AWQ g128: per-linear
+    mean inside one CUDA graph over > 2x L2 of distinct weight copies."""
+    m, k, n, gs = 16, 4096, 14336, 128
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    out = {}
+    for fmt in ("fp8", "awq"):
+        b, f = case_bytes_flops(m, k, n, fmt, gs)
+        wbytes = n * k if fmt == "fp8" else n * k // 2
+        copies = max(4, math.ceil(2 * l2 / wbytes))
+        g = torch.Generator(device=device).manual_seed(11)
+        ws = []
+        for _ in range(copies):
+            if fmt == "fp8":
+                codes = torch.randint(0, 126, (n, k), generator=g, device=device, dtype=torch.int16).to(torch.uint8)
+                sign = torch.randint(0, 2, (n, k), generator=g, device=device, dtype=torch.int16).to(torch.uint8) << 7
+                ws.append(((codes | sign).view(torch.float8_e4m3fn), torch.tensor([0.0003], device=device)))
+            else:
+                qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), generator=g, device=device,
+                                   dtype=torch.int64).to(torch.int32)
+                sc = (torch.rand(n, k // gs, generator=g, device=device) * 0.009 + 0.001).half()
+                z = torch.randint(0, 16, (n, k // gs), generator=g, device=device).half()
+                ws.append((qw, sc, z))
+        x = torch.randn(m, k, generator=g, device=device).to(torch.bfloat16)
+
+        def body():
+            for w in ws:
+                if fmt == "fp8":
+                    ops.fp8_linear(x, w[0], w[1])
+                else:
+                    ops.awq_linear(x, w[0], w[1], w[2], gs)
+        stream = torch.cuda.Stream(device)
+        with torch.cuda.stream(stream):
+            body()
+            body()
+        torch.cuda.synchronize()
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=stream):
+            body()
+        for _ in range(3):
+            gph.replay()
+        torch.cuda.synchronize()
+        reps = max(3, args.steps // 2)
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tot = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            s_ev.record()
+            gph.replay()
+            e_ev.record()
+            torch.cuda.synchronize()
+            tot += s_ev.elapsed_time(e_ev)
+        us = tot * 1e3 / (reps * copies)
+        gbs = b / (us * 1e-6) / 1e9
+        out[fmt] = {"workload": f"{fmt.upper()} M={m} K={k} N={n}" + (" g128" if fmt == "awq" else ""),
+                    "bytes_per_linear": b, "us_per_linear": round(us, 3), "achieved_gbs": round(gbs, 1),
+                    "frac": round(gbs / hbm, 4), "copies_in_graph": copies}
+        del gph, ws
+    out["peak_gbs"] = hbm
+    out["peak_source"] = f"{peak_src} HBM copy"
+    out["kernels"] = "FP8: tcgen05 decode kernel (kind::f8f6f4); AWQ at M <= 16: weight-ring mma.sync kernel"
+    out["method"] = "cold-L2 per-linear mean inside one CUDA graph, PDL"
+    return out
 
 
 def bench_awq_config0(torch, ops, device, args, peaks, peak_src, flush):
