@@ -495,7 +495,8 @@ def run_ours(args):
     tok_s = None
     if not args.no_model:
         tok_s = {"config2": bench_config2_tok_s(torch, dist, device, rank, world, args),
-                 "config3": bench_config3_tok_s(torch, dist, device, rank, world, args)}
+                 "config3": bench_config3_tok_s(torch, dist, device, rank, world, args),
+                 "config4": bench_config4_tok_s(torch, dist, device, rank, world, args)}
 
     host = measure_host_overhead(torch, ops, device) if world == 1 else None
 
@@ -667,6 +668,91 @@ def bench_config2_tok_s(torch, dist, device, rank, world, args):
             "decode_step_ms": round(step_ms, 4), "decode_step_batch": len(ps),
             "method": "packed prefill + one CUDA-graph replay per decode step (harness engine), fused q/k/v and "
                       "gate/up+SiLU launches at decode batch sizes; median of 3 runs after one warm-up"}
+
+
+def bench_config4_tok_s(torch, dist, device, rank, world, args):
+    """Qwen2.5-72B-shaped decoder, FP8 E4M3 on every
+    projection (random codes, built without dense projections), tensor
+    parallel over the N ranks: one prefill chunk of 8192 tokens (one
+    sequence, causal attention) and decode steps at a batch of 128 (context
+    2048, random cache), both timed on the device, max over ranks. Runs at
+    TP >= 2 (72 GB of weights plus the batch-128 cache exceed one GPU)."""
+    if world < 2:
+        return {"workload": "config 4: Qwen2.5-72B FP8", "skipped": "runs at TP 2/4/8 (72 GB of FP8 weights and a "
+                "44 GB batch-128 cache per 2 GPUs)"}
+    from harness import engine as E
+    from harness import model as H
+    from nanosglang_b200 import tensor_parallel as TP
+    cfg = H.QWEN2_5_72B
+    prompt, batch, ctx, steps = 8192, 128, 2048, 8
+    model = H.build_model_fp8(cfg, device=device, seed=7)
+    TP.tensor_parallel_model(model, world, rank)
+    torch.cuda.empty_cache()
+    wbytes = sum(b.numel() * b.element_size() for n, b in model.named_buffers() if n.endswith("weight_fp8"))
+    hd = cfg.head_dim
+    proj_params = cfg.num_hidden_layers * cfg.hidden_size * (
+        2 * cfg.num_attention_heads * hd + 2 * cfg.num_key_value_heads * hd + 3 * cfg.intermediate_size)
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # prefill: one 8192-token chunk into a one-slot cache
+    eng = E.DecodeEngine(model, max_slots=1, max_len=prompt + 8, max_steps=4)
+    g = torch.Generator(device=device).manual_seed(17)  # the same prompt on every rank
+    toks = torch.randint(0, cfg.vocab_size, (prompt,), generator=g, device=device)
+    eng.prefill([toks])
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = 2
+    s_ev.record()
+    for _ in range(reps):
+        eng.prefill([toks])
+    e_ev.record()
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(s_ev.elapsed_time(e_ev) / reps)
+    del eng
+    torch.cuda.empty_cache()
+    # decode: batch 128 at context 2048, one CUDA-graph replay per step
+    eng = E.DecodeEngine(model, max_slots=batch, max_len=ctx + steps + 8, max_steps=steps + 4)
+    gk = torch.Generator(device=device).manual_seed(19 + rank)
+    for kc, vc in eng.caches:
+        kc.normal_(generator=gk)
+        vc.normal_(generator=gk)
+    eng.capture([batch])
+    eng.tokens.copy_(torch.randint(0, cfg.vocab_size, (batch,), generator=g, device=device))
+    gph = eng.graphs[batch]
+
+    def run(n):
+        eng.positions.fill_(ctx)
+        eng.step.zero_()
+        for _ in range(n):
+            gph.replay()
+
+    run(2)
+    torch.cuda.synchronize()
+    dist.barrier()
+    eng.positions.fill_(ctx)
+    eng.step.zero_()
+    s_ev.record()
+    for _ in range(steps):
+        gph.replay()
+    e_ev.record()
+    torch.cuda.synchronize()
+    decode_ms = max_over_ranks(s_ev.elapsed_time(e_ev) / steps)
+    del gph, eng, model
+    torch.cuda.empty_cache()
+    return {"workload": "config 4: Qwen2.5-72B FP8 E4M3 (all projections), prefill chunk of 8192 tokens + decode "
+                        "batch of 128 at context 2048, bf16 activations",
+            "tp": world, "fp8_weight_bytes_per_rank": int(wbytes),
+            "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(prompt / (prefill_ms * 1e-3), 1),
+            "prefill_tflops": round(2.0 * prompt * proj_params / world / (prefill_ms * 1e-3) / 1e12, 1),
+            "decode_step_ms": round(decode_ms, 3), "decode_tok_s": round(batch / (decode_ms * 1e-3), 1),
+            "method": "harness engine: packed prefill (SDPA causal) timed twice after one warm-up; decode-step graph "
+                      "replayed 8 times; device time, max over ranks; prefill_tflops = the projections' 2 M N K per "
+                      "rank over the whole prefill time (attention, norms and all-reduces included)"}
 
 
 def bench_config3_tok_s(torch, dist, device, rank, world, args):

@@ -379,6 +379,43 @@ def init_dense(model: CausalLM, seed: int):
             lin.weight.copy_(_uniform(gen, lin.weight.shape, 1.0 / math.sqrt(lin.in_features), gen.device))
 
 
+def build_model_fp8(config: ModelConfig, device="cpu", dtype=torch.bfloat16, seed: int = 5) -> CausalLM:
+    """A model whose projections are nanosglang_b200 FP8Linear modules from the
+    start, for sizes whose dense projections never fit (Qwen2.5-72B: 140 GB in
+    bf16): the model is built on the meta device, every projection is replaced
+    by an FP8Linear there, and only then is memory allocated. Weights are
+    seeded random e4m3 codes (every finite code but the two largest, either
+    sign; no NaN codes) with a per-tensor scale that puts the largest at 0.06,
+    the range of N(0, 0.02) weights; the other weights as ``init_common``."""
+    from nanosglang_b200 import quantization as Q
+    with torch.device("meta"):
+        model = CausalLM(config)
+        for layer in model.layers:
+            for path in PROJECTIONS:
+                parent_path, name = path.rsplit(".", 1)
+                parent = layer.get_submodule(parent_path)
+                lin = getattr(parent, name)
+                setattr(parent, name, Q.FP8Linear(lin.in_features, lin.out_features, bias=lin.bias is not None))
+    model = model.to_empty(device=device)
+    cos, sin = precompute_rope_freqs(config.head_dim, config.max_position_embeddings, config.rope_theta,
+                                     device=device)
+    model.rope_cos, model.rope_sin = cos, sin
+    for p in model.parameters():
+        p.data = p.data.to(dtype)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        init_common(model, gen)
+        for layer in model.layers:
+            for path in PROJECTIONS:
+                m = layer.get_submodule(path)
+                codes = torch.randint(0, 126, m.weight_fp8.shape, generator=gen, device=device, dtype=torch.uint8)
+                sign = torch.randint(0, 2, m.weight_fp8.shape, generator=gen, device=device, dtype=torch.uint8)
+                m.weight_fp8.view(torch.uint8).copy_(codes | (sign << 7))
+                m.weight_scale.fill_(0.06 / 448.0)
+                del codes, sign
+    return model
+
+
 def awq_buffers(gen: torch.Generator, n: int, k: int, group_size: int = 128):
     """BASELINE config-0 distributions in the reference layout: int4 values
     uniform on 0..15 packed 8 per int32 along K (qweight [N, K/8]), zero
