@@ -58,3 +58,28 @@ def test_harness_decode_and_prefill_paths_match_batched_forward():
             full = m(seq[None], torch.arange(len(seq))[None], None, None,
                      H.causal_mask(len(seq), torch.float32, "cpu"))
             np.testing.assert_allclose(dec[i].numpy(), full[0, -1].numpy(), rtol=1e-4, atol=1e-5)
+
+
+def test_build_model_fp8_never_allocates_dense_projections():
+    """Config-4-sized models: every projection is an FP8Linear from the start
+    (meta-device build), codes are finite e4m3 of either sign, the scale puts
+    the largest at 0.06, and tensor-parallel sharding takes the modules as is."""
+    from nanosglang_b200 import quantization as Q
+    from nanosglang_b200 import tensor_parallel as TP
+    cfg = H.TINY
+    m = H.build_model_fp8(cfg, device="cpu", seed=3)
+    for layer in m.layers:
+        for path in H.PROJECTIONS:
+            mod = layer.get_submodule(path)
+            assert isinstance(mod, Q.FP8Linear) and not hasattr(mod, "weight")
+            codes = mod.weight_fp8.view(torch.uint8)
+            assert int((codes & 0x7F).max()) <= 125  # no NaN code (0x7F / 0xFF)
+            assert int(codes.max()) >= 128  # both signs
+            assert float(mod.weight_scale) == np.float32(0.06 / 448.0)
+    assert m.layers[0].self_attn.q_proj.bias.dtype == torch.bfloat16
+    again = H.build_model_fp8(cfg, device="cpu", seed=3)  # seeded
+    assert torch.equal(again.layers[1].mlp.down_proj.weight_fp8.view(torch.uint8),
+                       m.layers[1].mlp.down_proj.weight_fp8.view(torch.uint8))
+    TP.tensor_parallel_model(m, 2, 1)
+    q = m.layers[0].self_attn.q_proj
+    assert q.linear.weight_fp8.shape[0] == cfg.num_attention_heads * cfg.head_dim // 2
