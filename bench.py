@@ -39,8 +39,8 @@ JSON), for Nsight Compute captures of a small case (one kernel, <= 4 launches):
   down8192       FP8 down 4864->896 at M=8192 (the sweep's paired-kernel launch), 3 launches
   awq0           config-0 AWQ linear (M=16, K=896, N=9728), 4 launches
   awq_llama_gate / fp8_llama_gate   Llama-3-8B gate 4096->14336 at M=16, 3 launches
-  sweep_prefill / sweep_decode      the sweep's M > 64 (M <= 64) FP8 linears once each,
-                 for a per-launch DRAM traffic table (metrics of one pass only)
+  sweep_one      sweep linear --ncu-index i (0..41, shape-major, M fastest), 3 launches:
+                 one linear per capture for the per-launch DRAM traffic table
 """
 
 from __future__ import annotations
@@ -984,7 +984,7 @@ def run_reference(args):
         "e2e": {"value": round(r["value"], 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def run_ncu_case(name):
+def run_ncu_case(name, index=0):
     """A handful of launches of one kernel class, for an Nsight Compute capture."""
     import torch
 
@@ -1020,12 +1020,13 @@ def run_ncu_case(name):
             codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
             for _ in range(3):
                 ops.fp8_linear(x, codes, scale)
-    elif name in ("sweep_prefill", "sweep_decode"):
-        for _, k, n in SHAPES:
-            codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
-            for m in [mm for mm in MS if (mm <= 64) == (name == "sweep_decode")]:
-                x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
-                ops.fp8_linear(x, codes, scale)
+    elif name == "sweep_one":
+        _, k, n = SHAPES[index // len(MS)]
+        m = MS[index % len(MS)]
+        codes, scale, _ = ops.fp8_quantize((torch.randn(n, k, generator=g) * 0.02).to(dev))
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        for _ in range(3):
+            ops.fp8_linear(x, codes, scale)
     elif name == "awq0":
         m, k, n, gs = 16, 896, 9728, 128
         for _ in range(4):
@@ -1057,12 +1058,15 @@ def main():
                     help="row-parallel layers overlap chunked GEMMs with their all-reduces from this many tokens "
                          "(0: off, the default)")
     ap.add_argument("--ncu-case", choices=["prefill", "down8192", "awq0", "awq_llama_gate", "fp8_llama_gate",
-                                           "sweep_prefill", "sweep_decode"],
+                                           "sweep_one"],
                     default=None,
                     help="run a small case of one kernel class for a profiler capture, then exit")
+    ap.add_argument("--ncu-index", type=int, default=0, help="sweep_one: which of the 42 sweep linears (0..41)")
     args = ap.parse_args()
     if args.ncu_case:
-        run_ncu_case(args.ncu_case)
+        if not 0 <= args.ncu_index < len(SHAPES) * len(MS):
+            raise SystemExit("--ncu-index out of range")
+        run_ncu_case(args.ncu_case, args.ncu_index)
         return
     args.warmup = max(3, args.warmup)
     out = run_reference(args) if args.impl == "reference" else run_ours(args)
