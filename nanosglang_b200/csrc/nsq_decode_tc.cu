@@ -27,24 +27,26 @@
 //        the block's largest.
 // Integer products (AWQ) are exact; the accumulators are fp32 throughout.
 //
-// Work split: CTA i owns weight rows [i R, i R + R), R <= 128 (one TMA box per
-// k-block, TMEM lane = row), and the whole K range; no split-K, no workspace.
+// Work split: CTA i owns a block of weight rows, a multiple of 8 between 64 and
+// 128 (TMEM lane = row; one TMA box of [rows x 128 B] per ring slot), and the
+// whole K range: accumulators never leave the CTA, no split-K, no workspace.
 // Warp roles (AWQ 576 threads, FP8 448):
-//   warp 0      TMA producer (one lane): k-blocks of the weight rows, straight
-//               into the UMMA A ring (FP8), or pairs of k-blocks of packed
-//               nibbles into a raw ring (AWQ). Weights are static, so it never
-//               waits for the previous kernel.
+//   warp 0      TMA producer (one lane): one 128-byte chunk of every row per
+//               ring slot -- an FP8 k-block, which is the UMMA A tile itself,
+//               or two AWQ k-blocks of packed nibbles. Weights are static, so
+//               it never waits for the previous kernel.
 //   warp 1      TMEM owner and UMMA issuer: per k-block four UMMAs (M = 128,
 //               N = 2 MP, K = 32) into one of four accumulators, then commits
-//               that free the A block, the x-term tile and fill the accumulator.
+//               that free the A tile, the x-term tile and fill the accumulator.
 //   warps 2-9   x terms, two groups of four warps taking alternate k-blocks:
 //               x k-blocks by TMA, four ahead; per k-block and token the scale
 //               2^e, T1 and T2 in the UMMA B layout (K-major, 128-byte
 //               swizzle), and the per-token sums of the terms (AWQ zero point).
 //   warps 10-13 epilogue: warp w reads TMEM sub-partition w % 4 (32 rows)
 //               after every k-block and accumulates in registers.
-//   warps 14-17 (AWQ) nibble widening: raw ring -> A ring.
-// Every wait is bounded.
+//   warps 14-17 (AWQ) nibble widening: ring slot -> A tile.
+// Every wait is bounded. Measured performance and the variants that lost are
+// in the design notes (tensor-core decode kernel).
 #include <atomic>
 
 #include "nsq_common.cuh"
@@ -70,8 +72,8 @@ constexpr int kTcNX = 8;   // per-token scalars of a k-block
 constexpr int kTcNXR = 4;  // x k-blocks staged ahead of the x-term warps
 constexpr uint32_t kTcTmemCols = 256;
 
-constexpr int kTcMaxNS = 12;  // weight stages (upper bound; the plan sizes the ring to shared memory)
-constexpr int kTcMaxNA = 4;  // widened k-block tiles (AWQ)
+constexpr int kTcMaxNS = 12;  // weight ring slots (upper bound; the plan sizes the ring to shared memory)
+constexpr int kTcMaxNA = 4;   // widened k-block tiles (AWQ)
 constexpr int kTcSmemMax = 227 * 1024;
 
 // FP8: the weight ring holds the UMMA A tiles themselves (one 128-byte box of
@@ -83,8 +85,9 @@ struct TcCfg {
   static constexpr int kKPS = FMT == 0 ? 2 : 1;  // k-blocks per ring slot
 };
 
-// Fixed part of the shared-memory layout (after the weight rings, whose size
-// the plan chooses): x-term tiles, x k-blocks, per-token scalars, barriers.
+// Fixed part of the shared-memory layout (after the AWQ A tiles and the weight
+// ring, whose sizes the plan chooses): x-term tiles, x k-blocks, per-token
+// scalars, barriers.
 template <int MP>
 struct TcFixed {
   static constexpr int kBBytes = 2 * MP * 128;  // x-term tile: 2 MP rows (T1 rows, then T2 rows) x 128 B
@@ -114,10 +117,10 @@ struct TcParams {
   int bias_dtype;
   int rlo, nhi;  // weight rows per CTA: rlo + 8 for the first nhi CTAs, rlo for the others (multiples of 8)
   int nkb;       // k-blocks of 128 columns
-  int tile;      // bytes of one k-block tile of the tallest CTA: (rlo + 8) x 128 B
-  int ns;    // weight stages in the ring
-  int na;    // A tiles
-  int off_raw, off_fixed;  // weight ring; fixed part (TcFixed)
+  int tile;      // bytes of a ring slot / A tile: the tallest CTA's rows x 128 B
+  int ns;        // weight ring slots
+  int na;        // AWQ A tiles (0 for FP8, whose ring slots are the A tiles)
+  int off_raw, off_fixed;  // the weight ring; the fixed part (TcFixed)
 };
 
 // Instruction descriptor: AWQ kind::i8 (A u8, B s8, D s32), FP8 kind::f8f6f4
@@ -194,9 +197,9 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
   // afull / aempty (their UMMAs finished). bfull / bempty:
   // x-term tiles. dfull: an accumulator's UMMAs finished; dempty: its four
   // readers are done. xsfull / xsempty: the per-token scalars of a k-block.
-  // Tiles are `tile` bytes apart (rows rounded up to 8): a UMMA reads 128 rows
-  // from a tile's start, so the rows past this CTA's come from the next tile
-  // (their accumulator lanes are never read).
+  // Tiles are `tile` bytes apart (the tallest CTA's rows, a multiple of 8): a
+  // UMMA reads 128 rows from a tile's start, so the rows past this CTA's come
+  // from the next tile or the fixed part (their accumulator lanes are never read).
   uint64_t* wfull = bars;
   uint64_t* wempty = wfull + kTcMaxNS;
   uint64_t* afull = wempty + kTcMaxNS;
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
   const int r0 = i_cta * p.rlo + 8 * min(i_cta, p.nhi);
   const int rvalid = min(rows, p.N - r0);
   const CUtensorMap* wmap = i_cta < p.nhi ? &wmap_hi : &wmap_lo;
-  const uint32_t ctile = (uint32_t)rows * 128u;  // k-block tile pitch inside a weight stage
+  const uint32_t ctile = (uint32_t)rows * 128u;  // bytes one TMA box of this CTA's rows lands
   const int nkb = p.nkb;
 
   if (threadIdx.x == 0) {
@@ -412,6 +415,9 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
           o2[i / 4] = d01 | (d23 << 16);
         }
       }
+      // an infinite or NaN x makes the token's outputs NaN, as the reference's
+      // matmul would (the terms of such a block are meaningless)
+      if (E == 255) sc = __int_as_float(0x7FC00000);
       // term rows tok (T1) and MP + tok (T2) of the x-term tile
       const uint32_t bt = smem_u32(fx + F::kB + s * F::kBBytes);
 #pragma unroll
@@ -516,35 +522,56 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     // k-block h of a raw slot = 16-byte pieces 4h .. 4h + 3 of each 128-byte
     // row; piece rc (32 columns, 4 words) becomes pieces 2 rc, 2 rc + 1 of
     // the A tile: per word, the bytes of nibbles 0,2,4,6 then 1,3,5,7.
+    // Both k-blocks of a slot per pass: every load of the pass is issued
+    // before its stores, and one proxy fence covers the pass.
     const int t = threadIdx.x - kTcWarpUnp0 * 32;
     const int nst = (nkb + KPS - 1) / KPS;
-    const int items = rows * 4;
+    const int items = rows * 4;  // (row, piece) pairs of one k-block, at most 512
+    constexpr int kIt = 4;       // items per thread and k-block (512 / 128)
     for (int st = 0; st < nst && ok; ++st) {
       const int rs = st % NS;
       if (!(ok = mbar_wait(&wfull[rs], (st / NS) & 1, p.status, 89, abort_flag))) break;
       const uint32_t raw = smem_u32(smem + p.off_raw) + (uint32_t)rs * tile;
+      const int nh = min(KPS, nkb - KPS * st);  // k-blocks of this slot inside K
+      uint4 w[KPS][kIt];
+#pragma unroll
       for (int h = 0; h < KPS; ++h) {
+#pragma unroll
+        for (int j = 0; j < kIt; ++j) {
+          const int i = t + j * kTcUnpWarps * 32;
+          const int r = i >> 2, rc = i & 3;
+          w[h][j] = make_uint4(0u, 0u, 0u, 0u);
+          if (h < nh && i < items) w[h][j] = lds128(raw + (uint32_t)r * 128u + (((h * 4 + rc) ^ (r & 7)) << 4));
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < KPS; ++h) {
+        if (h >= nh) break;
         const int b = KPS * st + h;
-        if (b >= nkb) break;
         const int a = b % NA;
         if (b >= NA && !(ok = mbar_wait(&aempty[a], ((b / NA) - 1) & 1, p.status, 90, abort_flag))) break;
         const uint32_t dst = smem_u32(smem) + (uint32_t)a * tile;
-        for (int i = t; i < items; i += kTcUnpWarps * 32) {
-          const int r = i >> 2, rc = i & 3;
-          const uint32_t rowb = (uint32_t)r * 128u;
-          const uint4 w = lds128(raw + rowb + (((h * 4 + rc) ^ (r & 7)) << 4));
-          sts128(dst + rowb + (((2 * rc) ^ (r & 7)) << 4), w.x & 0x0F0F0F0Fu, (w.x >> 4) & 0x0F0F0F0Fu,
-                 w.y & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu);
-          sts128(dst + rowb + (((2 * rc + 1) ^ (r & 7)) << 4), w.z & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                 w.w & 0x0F0F0F0Fu, (w.w >> 4) & 0x0F0F0F0Fu);
+#pragma unroll
+        for (int j = 0; j < kIt; ++j) {
+          const int i = t + j * kTcUnpWarps * 32;
+          if (i < items) {
+            const int r = i >> 2, rc = i & 3;
+            const uint32_t rowb = (uint32_t)r * 128u;
+            const uint4 v = w[h][j];
+            sts128(dst + rowb + (((2 * rc) ^ (r & 7)) << 4), v.x & 0x0F0F0F0Fu, (v.x >> 4) & 0x0F0F0F0Fu,
+                   v.y & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu);
+            sts128(dst + rowb + (((2 * rc + 1) ^ (r & 7)) << 4), v.z & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
+                   v.w & 0x0F0F0F0Fu, (v.w >> 4) & 0x0F0F0F0Fu);
+          }
         }
-        fence_proxy_async_smem();  // the tile is read by the tensor core
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&afull[a]);
       }
       if (!ok) break;
+      fence_proxy_async_smem();  // the tiles are read by the tensor core
       __syncwarp();
-      if (lane == 0) mbar_arrive(&wempty[rs]);
+      if (lane == 0) {
+        for (int h = 0; h < nh; ++h) mbar_arrive(&afull[(KPS * st + h) % NA]);
+        mbar_arrive(&wempty[rs]);
+      }
     }
   }
 

@@ -346,6 +346,32 @@ def test_fp8_linear_tensor_core_decode(m, n, k, dtype, bias):
     assert _fp8_case(m, n, k, dtype, bias, seed=950 + m + n) <= GEMM_TOL
 
 
+@pytest.mark.parametrize("fmt", ["fp8", "awq"])
+def test_tensor_core_decode_nonfinite_x(fmt):
+    """An infinite x makes its token's outputs NaN (the reference's matmul gives inf/NaN there); the other
+    tokens are unaffected."""
+    from nanosglang_b200 import ops
+    m, n, k = 17, 9472, 1024
+    x = rand_x(m, k, torch.bfloat16, 77)
+    x[3, 500] = float("inf")
+    if fmt == "fp8":
+        rng = np.random.default_rng(78)
+        codes, scale = O.fp8_quantize((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+        y = ops.fp8_linear(x.cuda(), torch.from_numpy(codes).cuda().view(torch.float8_e4m3fn),
+                           torch.tensor(scale).cuda())
+        with np.errstate(invalid="ignore"):  # the oracle's own inf * 0 in row 3
+            ref = O.fp8_linear(_to_np(x), codes, scale)
+    else:
+        (qw, s, z), (tq, ts, tz) = rand_awq(n, k, 128, seed=79, zero_mode="int")
+        y = ops.awq_linear(x.cuda(), tq, ts, tz, 128)
+        with np.errstate(invalid="ignore"):
+            ref = O.awq_linear(_to_np(x), qw, s, z, k, 128)
+    yn = _to_np(y)
+    assert np.isnan(yn[3]).all()
+    keep = [i for i in range(m) if i != 3]
+    assert O.rel_fro(yn[keep], ref[keep]) <= GEMM_TOL
+
+
 def test_fp8_linear_tensor_core_decode_wide_range_x():
     """x spanning many binades within a k-block (per-token, per-k-block power-of-two scales of the terms)."""
     from nanosglang_b200 import ops
