@@ -292,15 +292,26 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     // and the Qwen2.5-0.5B shapes stay on the kernels below). AWQ group sizes
     // 32 and 64 run here for every M <= 32.
     const bool small_group = a.fmt == 0 && a.group_size % 128 != 0;
-    // Layers of 64-128 rows per SM: the tensor-core decode kernel (the UMMA
-    // reads the stored weight; x as two narrow terms) for FP8 at 2..32 tokens
-    // and AWQ at 17..32 tokens or on weights of 64 M+ elements (B200, CUDA-graph
-    // chains: FP8 4096 -> 14336 at M = 16 23.3 -> 21.3 us, M = 32 29.3 -> 24.4
-    // us; AWQ 8192 -> 18944 at M = 16 107 -> 56 us, 4096 -> 14336 at M = 32
-    // 37.2 -> 35.5 us; AWQ at M <= 16 on smaller weights stays on the
-    // weight-ring kernel, 23.9 vs 27.8 us)
-    if (a.M <= 32 && !small_group && decode_tc_rows(a) > 0 &&
-        (a.fmt == 1 ? a.M >= 2 : (a.M > 16 || (int64_t)a.K * a.N >= ((int64_t)1 << 26)))) {
+    // Layers of 64-128 rows per SM: the tensor-core decode kernel (x as two
+    // narrow terms; FP8 A read from the TMA tile, AWQ A widened into tensor
+    // memory). Where it wins (B200, CUDA-graph chains of distinct weights,
+    // PDL; us, tensor core vs the best other kernel):
+    //   FP8, K >= 2048, every M: 4096 -> 14336 17.8 vs 20.7 (M = 1), 18.0 vs
+    //   23.7 (16), 23.4 vs 30.0 (32); 8192 -> 18944 32.5 vs 38.3 (1).
+    //   FP8, K < 2048 (896 -> 9472, 1024 -> 10000): within 0.5 us either way;
+    //   it takes 9..16 and 25..32 tokens.
+    //   AWQ, K >= 2048: 25..32 tokens (4096 -> 14336 32.0 vs 37.9); 17..24
+    //   and 9..16 tokens on weights of 64 M / 56 M+ elements (3584 -> 18944
+    //   at M = 16 21.7 vs 23.9, 4096 -> 12288 stays on the weight ring, 21.7
+    //   vs 22.9); up to 8 tokens only where the weight ring does not fit
+    //   (8192 -> 18944: 51 us, no ring plan).
+    const int64_t kn = (int64_t)a.K * a.N;
+    const bool tc_wins =
+        a.fmt == 1 ? (a.K >= 2048 || (a.M > 8 && a.M <= 16) || a.M > 24)
+                   : a.K >= 2048 && (a.M > 24 || (a.M > 16   ? kn >= ((int64_t)1 << 26)
+                                                  : a.M > 8 ? kn >= ((int64_t)7 << 23)
+                                                            : kn >= ((int64_t)1 << 27)));
+    if (a.M <= 32 && !small_group && tc_wins && decode_tc_rows(a) > 0) {
       const int rc = run_decode_tc_linear(a, stream);
       if (rc != NSQ_ENOTSUP) return rc;
     }
@@ -314,8 +325,14 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     }
     const int ctas = decode_linear_ctas(a);
     if (ctas < 0 || ctas > 2 * num_sms()) {
-      const int rc = run_decode_stream_linear(a, stream);
+      int rc = run_decode_stream_linear(a, stream);
       if (rc != NSQ_ENOTSUP) return rc;
+      // no weight-ring plan (AWQ 8192 -> 29568 at M <= 16): the row-streaming
+      // kernel, not the multi-wave one (74 vs 122 us, B200)
+      if (a.M <= 32) {
+        rc = run_decode_rows_linear(a, stream);
+        if (rc != NSQ_ENOTSUP) return rc;
+      }
     }
     if (a.K <= 1024 && (a.M <= 8 || a.N <= 1024)) {
       const int rc = run_decode_wave_linear(a, stream);

@@ -1,7 +1,8 @@
 // Tensor-core decode linear (M <= 32 tokens) for layers of at least 64 rows per
-// SM: the tcgen05 UMMAs read the weight straight from the TMA-staged tiles, and
+// SM: the tcgen05 UMMAs take the weight from the TMA-staged tiles (FP8) or from
+// tensor memory, where four warps store the nibbles widened to bytes (AWQ), and
 // x enters the tensor core as two narrow terms, so no CUDA-core instruction
-// touches the weight values (FP8) or only widens nibbles to bytes (AWQ).
+// does arithmetic on a weight value (FP8) or more than widen nibbles (AWQ).
 //
 // Replaces AWQLinear.forward / FP8Linear.forward (nano_sglang/decode/
 // quantization.py:150-152 and :49-52) for small batches on large layers
@@ -30,21 +31,26 @@
 // Work split: CTA i owns a block of weight rows, a multiple of 8 between 64 and
 // 128 (TMEM lane = row; one TMA box of [rows x 128 B] per ring slot), and the
 // whole K range: accumulators never leave the CTA, no split-K, no workspace.
-// Warp roles (AWQ 576 threads, FP8 448):
+// Warp roles (FP8 448 threads, AWQ 576):
 //   warp 0      TMA producer (one lane): one 128-byte chunk of every row per
 //               ring slot -- an FP8 k-block, which is the UMMA A tile itself,
 //               or two AWQ k-blocks of packed nibbles. Weights are static, so
 //               it never waits for the previous kernel.
 //   warp 1      TMEM owner and UMMA issuer: per k-block four UMMAs (M = 128,
-//               N = 2 MP, K = 32) into one of four accumulators, then commits
-//               that free the A tile, the x-term tile and fill the accumulator.
+//               N = 2 MP, K = 32; A from the ring slot or the tensor-memory
+//               tile, B from shared memory) into one of four accumulators,
+//               then commits that free the A tile, the x-term tile and fill
+//               the accumulator.
 //   warps 2-9   x terms, two groups of four warps taking alternate k-blocks:
 //               x k-blocks by TMA, four ahead; per k-block and token the scale
 //               2^e, T1 and T2 in the UMMA B layout (K-major, 128-byte
 //               swizzle), and the per-token sums of the terms (AWQ zero point).
 //   warps 10-13 epilogue: warp w reads TMEM sub-partition w % 4 (32 rows)
 //               after every k-block and accumulates in registers.
-//   warps 14-17 (AWQ) nibble widening: ring slot -> A tile.
+//   warps 14-17 (AWQ) weight transfer: warp w takes TMEM sub-partition w % 4,
+//               one weight row per lane: the row's 128 bytes of a ring slot
+//               into registers (the slot is then free), nibbles widened to
+//               bytes, tcgen05.st into one of four tensor-memory A tiles.
 // Every wait is bounded. Measured performance and the variants that lost are
 // in the design notes (tensor-core decode kernel).
 #include <atomic>
@@ -64,30 +70,35 @@ constexpr int kTcPrepWarps = 8;
 constexpr int kTcXGroups = 2;  // x-term groups of four warps, alternating k-blocks
 constexpr int kTcWarpEpi0 = kTcWarpPrep0 + kTcPrepWarps;
 constexpr int kTcEpiWarps = 4;
-constexpr int kTcWarpUnp0 = kTcWarpEpi0 + kTcEpiWarps;
-constexpr int kTcUnpWarps = 4;
+constexpr int kTcWarpXfr0 = kTcWarpEpi0 + kTcEpiWarps;
+constexpr int kTcXfrWarps = 4;  // weight transfer: one per TMEM sub-partition
 constexpr int kTcND = 4;   // accumulators in TMEM
 constexpr int kTcNB = 4;   // x-term tiles
 constexpr int kTcNX = 8;   // per-token scalars of a k-block
 constexpr int kTcNXR = 4;  // x k-blocks staged ahead of the x-term warps
-constexpr uint32_t kTcTmemCols = 256;
+// Tensor memory: accumulators at columns d * 2 MP (d < kTcND); AWQ: tensor-
+// memory A tile t (t < kTcNA, 128 lanes x 128 bytes of widened weight) at
+// kTcTmemA + 32 t.
+constexpr int kTcNA = 4;
+constexpr uint32_t kTcTmemA = 256;
 
 constexpr int kTcMaxNS = 12;  // weight ring slots (upper bound; the plan sizes the ring to shared memory)
-constexpr int kTcMaxNA = 4;   // widened k-block tiles (AWQ)
 constexpr int kTcSmemMax = 227 * 1024;
 
-// FP8: the weight ring holds the UMMA A tiles themselves (one 128-byte box of
-// every row per k-block, straight from TMA); AWQ: the ring holds raw tiles of
-// packed nibbles (128 bytes of every row = two k-blocks), widened into A tiles.
+// A ring slot holds 128 bytes of every row: one FP8 k-block, or two AWQ
+// k-blocks of packed nibbles. FP8: the UMMAs read A straight from the ring
+// slot (shared memory); AWQ: transfer warps widen it into tensor memory and
+// the UMMAs read A there.
 template <int FMT>
 struct TcCfg {
-  static constexpr int kThreads = (FMT == 0 ? kTcWarpUnp0 + kTcUnpWarps : kTcWarpUnp0) * 32;
+  static constexpr bool kTmemA = FMT == 0;
+  static constexpr int kThreads = (kTmemA ? kTcWarpXfr0 + kTcXfrWarps : kTcWarpXfr0) * 32;
   static constexpr int kKPS = FMT == 0 ? 2 : 1;  // k-blocks per ring slot
+  static constexpr uint32_t kTmemCols = kTmemA ? 512 : 256;
 };
 
-// Fixed part of the shared-memory layout (after the AWQ A tiles and the weight
-// ring, whose sizes the plan chooses): x-term tiles, x k-blocks, per-token
-// scalars, barriers.
+// Fixed part of the shared-memory layout (after the weight ring, whose size
+// the plan chooses): x-term tiles, x k-blocks, per-token scalars, barriers.
 template <int MP>
 struct TcFixed {
   static constexpr int kBBytes = 2 * MP * 128;  // x-term tile: 2 MP rows (T1 rows, then T2 rows) x 128 B
@@ -96,12 +107,11 @@ struct TcFixed {
   static constexpr int kX = kB + kTcNB * kBBytes;
   static constexpr int kXs = kX + kTcNXR * kXBytes;  // [NX][2][MP] fp32: scale 2^e, term sum (AWQ)
   static constexpr int kBar = kXs + kTcNX * 2 * MP * 4;
-  static constexpr int kNumBars = 2 * kTcMaxNS + 2 * kTcMaxNA + 2 * kTcNB + 2 * kTcND + 2 * kTcNX + kTcNXR + 1;
+  static constexpr int kNumBars = 2 * kTcMaxNS + 2 * kTcNA + 2 * kTcNB + 2 * kTcND + 2 * kTcNX + kTcNXR + 1;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kBytes = ((kAbort + 4 + 1023) / 1024) * 1024;
   static_assert(kBBytes % 1024 == 0 && kXBytes % 1024 == 0, "tiles stay 1 KB aligned");
-  static_assert(kTcNB * kBBytes >= 16 * 1024, "the last UMMA A tile may read up to 16 KB past its start");
 };
 
 struct TcParams {
@@ -117,10 +127,9 @@ struct TcParams {
   int bias_dtype;
   int rlo, nhi;  // weight rows per CTA: rlo + 8 for the first nhi CTAs, rlo for the others (multiples of 8)
   int nkb;       // k-blocks of 128 columns
-  int tile;      // bytes of a ring slot / A tile: the tallest CTA's rows x 128 B
-  int ns;        // weight ring slots
-  int na;        // AWQ A tiles (0 for FP8, whose ring slots are the A tiles)
-  int off_raw, off_fixed;  // the weight ring; the fixed part (TcFixed)
+  int tile;       // bytes of a ring slot: the tallest CTA's rows x 128 B
+  int ns;         // weight ring slots (at shared-memory offset 0)
+  int off_fixed;  // the fixed part (TcFixed)
 };
 
 // Instruction descriptor: AWQ kind::i8 (A u8, B s8, D s32), FP8 kind::f8f6f4
@@ -130,28 +139,88 @@ __host__ __device__ constexpr uint32_t tc_idesc(int fmt, int m, int n) {
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-// The four UMMAs of one k-block (K = 32 each: 32 bytes of every 128-byte row
-// per step, +2 in descriptor units), issued by the elected lane of a converged
-// warp in one asm block; the first starts a fresh accumulator.
-template <int FMT>
-__device__ __forceinline__ void tc_umma_k128_elect(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc) {
-#define NSQ_TC_UMMA(KIND)                                                                        \
+// The four UMMAs of one k-block (K = 32 each), issued by the elected lane of a
+// converged warp in one asm block; the first starts a fresh accumulator. B is
+// the x-term tile (128-byte swizzle, +32 bytes = +2 descriptor units per
+// step). A is either a shared-memory tile (descriptor, same stepping; FP8) or
+// a tensor-memory tile at column ta (row i in lane i, 32 bytes = 8 columns per
+// step, bytes in K order; AWQ).
+// Cost (measured, Llama-3-8B gate at 16 tokens): with A in shared memory the
+// four UMMAs of a k-block keep the issuer about 0.43 us with every barrier
+// already passed (0.36 us with one UMMA instead of four, nearly the same at
+// half the N), so reading the 128 A rows, not the MACs, costs; tcgen05.cp of
+// the tile into tensor memory first is no faster (it reads the same rows).
+// With A in tensor memory the UMMAs are cheap but the transfer warps' loads,
+// stores and waits add about 0.6 us of latency per k-block: for FP8 that lost
+// (19.9 us against 17.7), for AWQ, whose nibbles need the warps anyway, it won
+// (22.7 us against 27.9, and 31.5 against 38.5 at 32 tokens).
+#define NSQ_TC_UMMA4(KIND, A0, A1, A2, A3, ACON, ...)                                             \
   asm volatile(                                                                                  \
       "{\n\t.reg .pred e, p, t;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"              \
       "setp.ne.b32 p, %9, %9;\n\tsetp.eq.b32 t, %9, %9;\n\t"                                     \
-      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %1, %5, %9, p;\n\t"                     \
-      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %2, %6, %9, t;\n\t"                     \
-      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %3, %7, %9, t;\n\t"                     \
-      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], %4, %8, %9, t;\n\t}" ::"r"(d),          \
-      "l"(a), "l"(a + 2), "l"(a + 4), "l"(a + 6), "l"(b), "l"(b + 2), "l"(b + 4), "l"(b + 6),  \
-      "r"(idesc)                                                                                 \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], " A0 ", %5, %9, p;\n\t"                 \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], " A1 ", %6, %9, t;\n\t"                 \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], " A2 ", %7, %9, t;\n\t"                 \
+      "@e tcgen05.mma.cta_group::1.kind::" KIND " [%0], " A3 ", %8, %9, t;\n\t}" ::"r"(d),      \
+      ACON(a), ACON(a + (__VA_ARGS__)), ACON(a + 2 * (__VA_ARGS__)), ACON(a + 3 * (__VA_ARGS__)), \
+      "l"(b), "l"(b + 2), "l"(b + 4), "l"(b + 6), "r"(idesc)                                      \
       : "memory")
-  if constexpr (FMT == 0) {
-    NSQ_TC_UMMA("i8");
-  } else {
-    NSQ_TC_UMMA("f8f6f4");
-  }
-#undef NSQ_TC_UMMA
+#define NSQ_TC_R(x) "r"(x)
+#define NSQ_TC_L(x) "l"(x)
+// A in shared memory (descriptor a)
+__device__ __forceinline__ void tc_umma_ss_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc) {
+  NSQ_TC_UMMA4("f8f6f4", "%1", "%2", "%3", "%4", NSQ_TC_L, 2);
+}
+// A in tensor memory (column a)
+__device__ __forceinline__ void tc_umma_ts_i8(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc) {
+  NSQ_TC_UMMA4("i8", "[%1]", "[%2]", "[%3]", "[%4]", NSQ_TC_R, 8);
+}
+#undef NSQ_TC_UMMA4
+#undef NSQ_TC_R
+#undef NSQ_TC_L
+
+// Three commits from the elected lane in one asm block: each barrier gets one
+// arrival once every tcgen05 op this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit3_elect(uint64_t* a, uint64_t* b, uint64_t* c) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%1];\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%2];\n\t}" ::"r"(smem_u32(a)),
+      "r"(smem_u32(b)), "r"(smem_u32(c))
+      : "memory");
+}
+
+// Non-blocking probe of three barrier phases in one asm block (the three
+// reads overlap): true if all three have completed. The callers fall back to
+// the bounded waits one by one when it returns false.
+// Why: the UMMA issuer's three blocking waits in a row cost it about 0.1 us
+// per k-block even with every phase long completed (measured: the FP8 gate of
+// Llama-3-8B at 16 tokens went from 21.2 to 18.0 us with this probe first).
+__device__ __forceinline__ bool mbar_test3(uint64_t* a, uint32_t pa, uint64_t* b, uint32_t pb, uint64_t* c,
+                                           uint32_t pc) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p, q, r;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 q, [%3], %4;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 r, [%5], %6;\n\t"
+      "and.pred p, p, q;\n\tand.pred p, p, r;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(a)), "r"(pa), "r"(smem_u32(b)), "r"(pb), "r"(smem_u32(c)), "r"(pc)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking probe of one barrier phase.
+__device__ __forceinline__ bool mbar_test1(uint64_t* a, uint32_t pa) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(a)), "r"(pa)
+      : "memory");
+  return ok != 0;
 }
 
 // One rank-3 TMA box into shared memory (no multicast), completing on `bar`.
@@ -192,19 +261,18 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* fx = smem + p.off_fixed;
   uint64_t* bars = reinterpret_cast<uint64_t*>(fx + F::kBar);
-  // Weight ring (one box of 128 bytes of every row per slot, filled by TMA):
-  // wfull / wempty. AWQ A tiles (one k-block each, widened from the ring):
-  // afull / aempty (their UMMAs finished). bfull / bempty:
-  // x-term tiles. dfull: an accumulator's UMMAs finished; dempty: its four
-  // readers are done. xsfull / xsempty: the per-token scalars of a k-block.
-  // Tiles are `tile` bytes apart (the tallest CTA's rows, a multiple of 8): a
-  // UMMA reads 128 rows from a tile's start, so the rows past this CTA's come
-  // from the next tile or the fixed part (their accumulator lanes are never read).
+  // Weight ring (one box of 128 bytes of every row per slot, filled by TMA;
+  // slots `tile` bytes apart, the tallest CTA's rows): wfull / wempty (the
+  // four transfer warps have the slot in registers). Tensor-memory A tiles:
+  // afull (four transfer warps stored) / aempty (their UMMAs finished).
+  // bfull / bempty: x-term tiles. dfull: an accumulator's UMMAs finished;
+  // dempty: its four readers are done. xsfull / xsempty: the per-token
+  // scalars of a k-block.
   uint64_t* wfull = bars;
   uint64_t* wempty = wfull + kTcMaxNS;
   uint64_t* afull = wempty + kTcMaxNS;
-  uint64_t* aempty = afull + kTcMaxNA;
-  uint64_t* bfull = aempty + kTcMaxNA;
+  uint64_t* aempty = afull + kTcNA;
+  uint64_t* bfull = aempty + kTcNA;
   uint64_t* bempty = bfull + kTcNB;
   uint64_t* dfull = bempty + kTcNB;
   uint64_t* dempty = dfull + kTcND;
@@ -216,7 +284,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
   volatile int* abort_flag = reinterpret_cast<volatile int*>(fx + F::kAbort);
   float* xs = reinterpret_cast<float*>(fx + F::kXs);
   constexpr int KPS = TcCfg<FMT>::kKPS;
-  const int NS = p.ns, NA = p.na;
+  const int NS = p.ns;
   const uint32_t tile = (uint32_t)p.tile;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -232,10 +300,10 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     *abort_flag = 0;
     for (int i = 0; i < NS; ++i) {
       mbar_init(&wfull[i], 1);
-      mbar_init(&wempty[i], FMT == 0 ? kTcUnpWarps : 1);
+      mbar_init(&wempty[i], TcCfg<FMT>::kTmemA ? kTcXfrWarps : 1);
     }
-    for (int i = 0; i < NA; ++i) {
-      mbar_init(&afull[i], kTcUnpWarps);
+    for (int i = 0; i < kTcNA; ++i) {
+      mbar_init(&afull[i], kTcXfrWarps);
       mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < kTcNB; ++i) {
@@ -255,7 +323,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     fence_barrier_init();
   }
   if (warp == kTcWarpMma) {
-    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_alloc(tmem_slot, TcCfg<FMT>::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -273,7 +341,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
       // row read zeros; their k-blocks are never used.
       tma_prefetch_desc(wmap);
       const int nst = (nkb + KPS - 1) / KPS;
-      uint8_t* ring = smem + p.off_raw;
+      uint8_t* ring = smem;
       int st = 0;
       for (; st < nst; ++st) {
         const int slot = st % NS;
@@ -289,26 +357,32 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     // ---------------- UMMA issuer (whole warp, converged) ----------------
     const uint32_t idesc = tc_idesc(FMT, kTcM, 2 * MP);
     for (int b = 0; b < nkb; ++b) {
-      const int s = b % kTcNB, d = b % kTcND;
-      // the A tile of k-block b: FP8 ring slot b % ns; AWQ widened tile b % na
-      const int a = FMT == 1 ? b % NS : b % NA;
-      if constexpr (FMT == 1) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&wfull[a], (b / NS) & 1, p.status, 81, abort_flag));
-      } else {
-        ok = __all_sync(0xffffffffu, mbar_wait(&afull[a], (b / NA) & 1, p.status, 82, abort_flag));
+      const int s = b % kTcNB, d = b % kTcND;  // x-term tile, accumulator
+      // the A tile: FP8 ring slot b % ns; AWQ tensor-memory tile b % kTcNA
+      const int a = FMT == 1 ? b % NS : b % kTcNA;
+      uint64_t* abar = FMT == 1 ? &wfull[a] : &afull[a];
+      const uint32_t apar = FMT == 1 ? ((b / NS) & 1) : ((b / kTcNA) & 1);
+      const uint32_t bpar = (b / kTcNB) & 1;
+      const uint32_t dpar = ((b / kTcND) - 1) & 1;  // accumulator d free again (k-block b - kTcND read out)
+      // the A tile, the x-term tile and the accumulator
+      const bool ready = __all_sync(
+          0xffffffffu, mbar_test3(abar, apar, &bfull[s], bpar, b >= kTcND ? &dempty[d] : &bfull[s], b >= kTcND ? dpar : bpar));
+      if (!ready) {
+        ok = __all_sync(0xffffffffu, mbar_wait(abar, apar, p.status, FMT == 1 ? 81 : 82, abort_flag));
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bfull[s], bpar, p.status, 83, abort_flag));
+        if (ok && b >= kTcND) ok = __all_sync(0xffffffffu, mbar_wait(&dempty[d], dpar, p.status, 84, abort_flag));
+        if (!ok) break;
       }
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bfull[s], (b / kTcNB) & 1, p.status, 83, abort_flag));
-      if (ok && b >= kTcND) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&dempty[d], ((b / kTcND) - 1) & 1, p.status, 84, abort_flag));
-      }
-      if (!ok) break;
       tc_fence_after();
-      const uint64_t adesc = sw128_kmajor_desc(smem_u32(smem + (FMT == 1 ? p.off_raw : 0)) + (uint32_t)a * tile);
       const uint64_t bdesc = sw128_kmajor_desc(smem_u32(fx + F::kB + s * F::kBBytes));
-      tc_umma_k128_elect<FMT>(tmem_base + (uint32_t)(d * 2 * MP), adesc, bdesc, idesc);
-      tc_commit_elect(FMT == 1 ? &wempty[a] : &aempty[a]);
-      tc_commit_elect(&bempty[s]);
-      tc_commit_elect(&dfull[d]);
+      const uint32_t dt = tmem_base + (uint32_t)(d * 2 * MP);
+      if constexpr (FMT == 1) {
+        tc_umma_ss_f8(dt, sw128_kmajor_desc(smem_u32(smem) + (uint32_t)a * tile), bdesc, idesc);
+        tc_commit3_elect(&wempty[a], &bempty[s], &dfull[d]);
+      } else {
+        tc_umma_ts_i8(dt, tmem_base + kTcTmemA + 32u * (uint32_t)a, bdesc, idesc);
+        tc_commit3_elect(&aempty[a], &bempty[s], &dfull[d]);
+      }
     }
     // every UMMA issued has finished before TMEM is released
     tc_commit_elect(mdone);
@@ -341,9 +415,15 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     const uint32_t xsrc0 = (uint32_t)((xc0 >> 6) * (F::kXBytes / 2) + tok * 128 + (xc0 & 63) * 2);
     for (int b = grp; b < nkb; b += kTcXGroups) {
       const int s = b % kTcNB, xsl = b % kTcNX, xr = b % kTcNXR;
-      if (b >= kTcNB && !(ok = mbar_wait(&bempty[s], ((b / kTcNB) - 1) & 1, p.status, 85, abort_flag))) break;
-      if (b >= kTcNX && !(ok = mbar_wait(&xsempty[xsl], ((b / kTcNX) - 1) & 1, p.status, 86, abort_flag))) break;
-      if (!(ok = mbar_wait(&xfull[xr], (b / kTcNXR) & 1, p.status, 91, abort_flag))) break;
+      const uint32_t xpar = (b / kTcNXR) & 1;
+      // the x-term tile and the scalar slot free, the x k-block landed
+      if (!mbar_test3(b >= kTcNB ? &bempty[s] : &xfull[xr], b >= kTcNB ? (((b / kTcNB) - 1) & 1) : xpar,
+                      b >= kTcNX ? &xsempty[xsl] : &xfull[xr], b >= kTcNX ? (((b / kTcNX) - 1) & 1) : xpar, &xfull[xr],
+                      xpar)) {
+        if (b >= kTcNB && !(ok = mbar_wait(&bempty[s], ((b / kTcNB) - 1) & 1, p.status, 85, abort_flag))) break;
+        if (b >= kTcNX && !(ok = mbar_wait(&xsempty[xsl], ((b / kTcNX) - 1) & 1, p.status, 86, abort_flag))) break;
+        if (!(ok = mbar_wait(&xfull[xr], xpar, p.status, 91, abort_flag))) break;
+      }
       const uint32_t xsrc = smem_u32(fx + F::kX + xr * F::kXBytes) + xsrc0;
       uint4 v[EPT / 8];
 #pragma unroll
@@ -451,7 +531,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
         mbar_wait(&xfull[bb % kTcNXR], (bb / kTcNXR) & 1, nullptr, 0, nullptr);
       }
     }
-  } else if (warp < kTcWarpUnp0) {
+  } else if (warp < kTcWarpXfr0) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;  // TMEM sub-partition: rows 32 q .. 32 q + 31
     const int row = q * 32 + lane;
@@ -517,68 +597,77 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
         }
       }
     }
-  } else if constexpr (FMT == 0) {
-    // ---------------- nibble widening (AWQ) ----------------
-    // k-block h of a raw slot = 16-byte pieces 4h .. 4h + 3 of each 128-byte
-    // row; piece rc (32 columns, 4 words) becomes pieces 2 rc, 2 rc + 1 of
-    // the A tile: per word, the bytes of nibbles 0,2,4,6 then 1,3,5,7.
-    // Both k-blocks of a slot per pass: every load of the pass is issued
-    // before its stores, and one proxy fence covers the pass.
-    const int t = threadIdx.x - kTcWarpUnp0 * 32;
+  } else if constexpr (TcCfg<FMT>::kTmemA) {
+    // ---------------- AWQ weight transfer: ring slot -> tensor-memory A tiles ----------------
+    // Lane i of warp w holds weight row 32 (w % 4) + i (its TMEM lane). A ring
+    // slot is two k-blocks; the row's 128 bytes are 16-byte chunks c at
+    // ((c ^ (row & 7)) << 4) (128-byte swizzle), k-block h = chunks 4h .. 4h + 3.
+    // Chunk rc of a k-block (32 columns of nibbles) becomes columns
+    // 8 rc .. 8 rc + 7 of its A tile: per word the bytes of nibbles 0,2,4,6
+    // (w & 0x0F0F0F0F), then 1,3,5,7 ((w >> 4) & 0x0F0F0F0F), the order the x
+    // terms are packed in. Rows past the CTA's store zeros (their accumulator
+    // lanes are never read). Per slot: all loads, both k-blocks' stores, one
+    // tcgen05.wait::st.
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool rin = row < rows;
+    const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16);  // this warp's 32 lanes
     const int nst = (nkb + KPS - 1) / KPS;
-    const int items = rows * 4;  // (row, piece) pairs of one k-block, at most 512
-    constexpr int kIt = 4;       // items per thread and k-block (512 / 128)
     for (int st = 0; st < nst && ok; ++st) {
-      const int rs = st % NS;
-      if (!(ok = mbar_wait(&wfull[rs], (st / NS) & 1, p.status, 89, abort_flag))) break;
-      const uint32_t raw = smem_u32(smem + p.off_raw) + (uint32_t)rs * tile;
-      const int nh = min(KPS, nkb - KPS * st);  // k-blocks of this slot inside K
-      uint4 w[KPS][kIt];
-#pragma unroll
-      for (int h = 0; h < KPS; ++h) {
-#pragma unroll
-        for (int j = 0; j < kIt; ++j) {
-          const int i = t + j * kTcUnpWarps * 32;
-          const int r = i >> 2, rc = i & 3;
-          w[h][j] = make_uint4(0u, 0u, 0u, 0u);
-          if (h < nh && i < items) w[h][j] = lds128(raw + (uint32_t)r * 128u + (((h * 4 + rc) ^ (r & 7)) << 4));
-        }
+      const int rs = st % NS, b0 = KPS * st, nb = min(KPS, nkb - b0);
+      const uint32_t wpar = (st / NS) & 1;
+      if (!__all_sync(0xffffffffu, mbar_test1(&wfull[rs], wpar))) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&wfull[rs], wpar, p.status, 89, abort_flag));
+        if (!ok) break;
       }
+      const uint32_t src = smem_u32(smem) + (uint32_t)rs * tile + (uint32_t)row * 128u;
+      uint4 w[8];
 #pragma unroll
-      for (int h = 0; h < KPS; ++h) {
-        if (h >= nh) break;
-        const int b = KPS * st + h;
-        const int a = b % NA;
-        if (b >= NA && !(ok = mbar_wait(&aempty[a], ((b / NA) - 1) & 1, p.status, 90, abort_flag))) break;
-        const uint32_t dst = smem_u32(smem) + (uint32_t)a * tile;
-#pragma unroll
-        for (int j = 0; j < kIt; ++j) {
-          const int i = t + j * kTcUnpWarps * 32;
-          if (i < items) {
-            const int r = i >> 2, rc = i & 3;
-            const uint32_t rowb = (uint32_t)r * 128u;
-            const uint4 v = w[h][j];
-            sts128(dst + rowb + (((2 * rc) ^ (r & 7)) << 4), v.x & 0x0F0F0F0Fu, (v.x >> 4) & 0x0F0F0F0Fu,
-                   v.y & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu);
-            sts128(dst + rowb + (((2 * rc + 1) ^ (r & 7)) << 4), v.z & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
-                   v.w & 0x0F0F0F0Fu, (v.w >> 4) & 0x0F0F0F0Fu);
-          }
+      for (int c = 0; c < 8; ++c) w[c] = rin ? lds128(src + ((c ^ (row & 7)) << 4)) : make_uint4(0u, 0u, 0u, 0u);
+      fence_proxy_async_smem();  // these reads precede the slot's next TMA write
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[rs]);
+      // the UMMAs of k-block b - kTcNA have read tile b % kTcNA
+      for (int j = 0; j < nb; ++j) {
+        const int b = b0 + j;
+        if (b < kTcNA) continue;
+        const uint32_t apar = ((b / kTcNA) - 1) & 1;
+        if (!__all_sync(0xffffffffu, mbar_test1(&aempty[b % kTcNA], apar))) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&aempty[b % kTcNA], apar, p.status, 90, abort_flag));
+          if (!ok) break;
         }
       }
       if (!ok) break;
-      fence_proxy_async_smem();  // the tiles are read by the tensor core
+      tc_fence_after();
+#pragma unroll
+      for (int h = 0; h < KPS; ++h) {
+        if (h >= nb) break;
+        uint32_t v0[16], v1[16];
+#pragma unroll
+        for (int rc = 0; rc < 4; ++rc) {
+          const uint4 u = w[4 * h + rc];
+          uint32_t* o = rc < 2 ? v0 + 8 * rc : v1 + 8 * (rc - 2);
+          o[0] = u.x & 0x0F0F0F0Fu, o[1] = (u.x >> 4) & 0x0F0F0F0Fu;
+          o[2] = u.y & 0x0F0F0F0Fu, o[3] = (u.y >> 4) & 0x0F0F0F0Fu;
+          o[4] = u.z & 0x0F0F0F0Fu, o[5] = (u.z >> 4) & 0x0F0F0F0Fu;
+          o[6] = u.w & 0x0F0F0F0Fu, o[7] = (u.w >> 4) & 0x0F0F0F0Fu;
+        }
+        const uint32_t ta = tl + kTcTmemA + 32u * (uint32_t)((b0 + h) % kTcNA);
+        tmem_st_32x32b_x16(ta, v0);
+        tmem_st_32x32b_x16(ta + 16, v1);
+      }
+      tmem_st_wait();
+      tc_fence_before();  // the stores precede the UMMAs that the arrivals release
       __syncwarp();
       if (lane == 0) {
-        for (int h = 0; h < nh; ++h) mbar_arrive(&afull[(KPS * st + h) % NA]);
-        mbar_arrive(&wempty[rs]);
+        for (int j = 0; j < nb; ++j) mbar_arrive(&afull[(b0 + j) % kTcNA]);
       }
     }
   }
-
   __syncthreads();
   if (warp == kTcWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTcTmemCols);
+    tmem_dealloc(tmem_base, TcCfg<FMT>::kTmemCols);
   }
 }
 
@@ -664,18 +753,14 @@ int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
   p.rlo = rlo;
   p.nhi = nhi;
   p.nkb = a.K / 128;
-  // Shared memory: AWQ A tiles, the weight ring (sized to what is left, at
-  // most kTcMaxNS slots), the fixed part. A UMMA reads 128 rows from a tile's
-  // start, so the rows past this CTA's come from the next tile (their
-  // accumulator lanes are never read).
+  // Shared memory: the weight ring (sized to what is left, at most kTcMaxNS
+  // slots of the tallest CTA's rows x 128 B), then the fixed part.
   p.tile = rmax * 128;
   const int fixed = mp == 16 ? TcFixed<16>::kBytes : TcFixed<32>::kBytes;
   const int room = kTcSmemMax - 1024 - fixed;
-  p.na = a.fmt == 0 ? kTcMaxNA : 0;
-  p.ns = (room - p.na * p.tile) / p.tile;
+  p.ns = room / p.tile;
   if (p.ns > kTcMaxNS) p.ns = kTcMaxNS;
-  p.off_raw = p.na * p.tile;
-  p.off_fixed = p.off_raw + p.ns * p.tile;
+  p.off_fixed = p.ns * p.tile;
   if (p.ns < 4) return NSQ_ENOTSUP;
   // weights as 32-bit words [N rows x K/8 (AWQ) or K/4 (FP8)], boxes of
   // [rows of the CTA x 32 words = 128 B], 128-byte swizzle

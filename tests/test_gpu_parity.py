@@ -197,14 +197,15 @@ def test_awq_linear_decode_large_layer(m):
 
 
 @pytest.mark.parametrize("m,n,k,gs,zm,dtype,bias", [
-    (17, 10000, 2048, 128, "int", torch.bfloat16, True),    # 64 / 72 rows per CTA
+    (25, 10000, 2048, 128, "int", torch.bfloat16, True),    # 64 / 72 rows per CTA
     (32, 14336, 4096, 256, "frac", torch.bfloat16, False),  # groups of two k-blocks, fractional zero points
-    (24, 12288, 1536, 128, "int", torch.float16, True),
-    (16, 18944, 4096, 128, "int", torch.bfloat16, False),   # 128 rows per CTA; 64 M+ weight elements at M = 16
-    (5, 18944, 4096, 128, "frac", torch.bfloat16, False)])
+    (28, 12288, 2048, 128, "int", torch.float16, True),
+    (16, 18944, 4096, 128, "int", torch.bfloat16, False),   # 128 rows per CTA; 56 M+ weight elements at M = 16
+    (5, 18944, 8192, 128, "frac", torch.bfloat16, False)])  # few tokens on a weight with no weight-ring plan
 def test_awq_linear_tensor_core_decode(m, n, k, gs, zm, dtype, bias):
-    """Layers of 64-128 rows per SM at M <= 32: the tcgen05 decode kernel (nibbles widened to u8, x as two s8
-    terms per k-block, kind::i8 UMMAs, zero point and scale per k-block in the epilogue)."""
+    """Layers of 64-128 rows per SM at M <= 32, shapes the dispatch sends to the tcgen05 decode kernel (nibbles
+    widened to u8 in tensor memory, x as two s8 terms per k-block, kind::i8 UMMAs, zero point and scale per k-block
+    in the epilogue)."""
     err = _awq_case(m, n, k, gs, dtype, bias, zm, seed=900 + m + n)
     assert err <= GEMM_TOL, err
 
@@ -336,13 +337,13 @@ def test_fp8_linear_decode_large_layer(m):
 
 
 @pytest.mark.parametrize("m,n,k,dtype,bias", [
-    (2, 9472, 1024, torch.bfloat16, False),   # 64 rows per CTA
+    (2, 9472, 2048, torch.bfloat16, False),   # 64 rows per CTA
     (13, 10000, 896, torch.bfloat16, True),   # 64 / 72 rows per CTA, K of seven k-blocks
     (16, 14336, 4096, torch.float16, True),
     (32, 18944, 2048, torch.bfloat16, False)])  # 128 rows per CTA
 def test_fp8_linear_tensor_core_decode(m, n, k, dtype, bias):
-    """Layers of 64-128 rows per SM at 2..32 tokens: the tcgen05 decode kernel (kind::f8f6f4 UMMAs on the stored
-    e4m3 codes, x as two e4m3 terms per token and k-block)."""
+    """Layers of 64-128 rows per SM, shapes the dispatch sends to the tcgen05 decode kernel (kind::f8f6f4 UMMAs on
+    the stored e4m3 codes, x as two e4m3 terms per token and k-block)."""
     assert _fp8_case(m, n, k, dtype, bias, seed=950 + m + n) <= GEMM_TOL
 
 
@@ -351,7 +352,7 @@ def test_tensor_core_decode_nonfinite_x(fmt):
     """An infinite x makes its token's outputs NaN (the reference's matmul gives inf/NaN there); the other
     tokens are unaffected."""
     from nanosglang_b200 import ops
-    m, n, k = 17, 9472, 1024
+    m, n, k = 26, 9472, 2048  # the tensor-core decode kernel for both formats
     x = rand_x(m, k, torch.bfloat16, 77)
     x[3, 500] = float("inf")
     if fmt == "fp8":
@@ -376,7 +377,7 @@ def test_fp8_linear_tensor_core_decode_wide_range_x():
     """x spanning many binades within a k-block (per-token, per-k-block power-of-two scales of the terms)."""
     from nanosglang_b200 import ops
     rng = np.random.default_rng(31)
-    n, k, m = 9472, 1024, 8
+    n, k, m = 9472, 2048, 8
     w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
     codes, scale = O.fp8_quantize(w)
     x = (rng.standard_normal((m, k)) * np.exp2(rng.integers(-12, 12, (m, k)))).astype(np.float32)
