@@ -916,7 +916,8 @@ def bench_decode_large(torch, ops, device, args, peaks, peak_src, flush):
         del gph, ws
     out["peak_gbs"] = hbm
     out["peak_source"] = f"{peak_src} HBM copy"
-    out["kernels"] = "FP8: tcgen05 decode kernel (kind::f8f6f4); AWQ at M <= 16: weight-ring mma.sync kernel"
+    out["kernels"] = ("tcgen05 decode kernel: FP8 kind::f8f6f4 with A from the TMA-staged tile; AWQ kind::i8 with "
+                      "the nibbles widened into tensor memory")
     out["method"] = "cold-L2 per-linear mean inside one CUDA graph, PDL"
     return out
 
