@@ -68,13 +68,25 @@ int nsq_awq_dequant(const int32_t* qweight, const uint16_t* scales, const uint16
                     uint16_t* w_out, int64_t N, int64_t K, int64_t group_size, void* stream);
 
 /*
+ * Workspace bytes with which nsq_awq_linear (quant 0) / nsq_fp8_linear
+ * (quant 1) of this shape runs its faster form: 0 when the call needs none.
+ * The workspace holds x converted for the tensor-core decode kernel (two
+ * narrow terms and a scale per token and 128-column block), written by a
+ * small kernel the call launches ahead of the linear. No counterpart in the
+ * reference.
+ */
+size_t nsq_linear_workspace_size(int quant, int64_t M, int64_t K, int64_t N, int64_t group_size);
+
+/*
  * AWQ W4A16 linear:  y = x @ dequant(qweight, scales, zeros)^T + bias.
  * Replaces AWQLinear.forward (quantization.py:150-152). x_dtype is F16 or
  * BF16 (y has the same dtype; the reference accepts fp16 only and raises on
  * bf16). bias_dtype is NONE/F16/BF16/F32. Requires K % 32 == 0,
  * group_size % 128 == 0, x/y/qweight 16-byte aligned.
- * M <= 64 runs the split-K tensor-core GEMV (workspace unused); larger M runs
- * the tcgen05 GEMM. Workspace may be NULL (none is needed by either).
+ * M <= 64 runs a decode kernel, larger M the tcgen05 GEMM. Workspace may be
+ * NULL; with nsq_linear_workspace_size() bytes (16-byte aligned, stream-
+ * ordered like y) the tensor-core decode kernel takes x in a precomputed form
+ * instead of every CTA converting it.
  */
 int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
                    const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
@@ -86,7 +98,7 @@ int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
  * Replaces FP8Linear.forward (quantization.py:49-52). weight_scale points to
  * ONE fp32 on the device (the reference's 0-dim / [1] buffer) and is read on
  * the device, never on the host. Requires K % 16 == 0, x/y/weight 16-byte
- * aligned. Workspace may be NULL.
+ * aligned. Workspace: as for nsq_awq_linear.
  */
 int nsq_fp8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
                    const uint8_t* weight_fp8, const float* weight_scale, const void* bias,

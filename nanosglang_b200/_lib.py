@@ -58,6 +58,7 @@ SIGNATURES = {
     "nsq_awq_from_autoawq": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                      c_void_p, c_void_p]),
     "nsq_fp8_quantize_workspace_size": (c_size_t, [c_int64, c_int64]),
+    "nsq_linear_workspace_size": (c_size_t, [c_int, c_int64, c_int64, c_int64, c_int64]),
     "nsq_fp8_quantize": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_size_t,
                                  c_void_p]),
     "nsq_fp8_quantize_noalloc": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),

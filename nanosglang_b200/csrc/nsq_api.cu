@@ -265,6 +265,30 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
   return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
 }
 
+// Layers of 64-128 rows per SM: the tensor-core decode kernel (x as two
+// narrow terms; FP8 A read from the TMA tile, AWQ A widened into tensor
+// memory). Where it wins (B200, CUDA-graph chains of distinct weights,
+// PDL; us, tensor core vs the best other kernel):
+//   FP8, K >= 2048, every M: 4096 -> 14336 17.8 vs 20.7 (M = 1), 18.0 vs
+//   23.7 (16), 23.4 vs 30.0 (32); 8192 -> 18944 32.5 vs 38.3 (1).
+//   FP8, K < 2048 (896 -> 9472, 1024 -> 10000): within 0.5 us either way;
+//   it takes 9..16 and 25..32 tokens.
+//   AWQ, K >= 2048: 25..32 tokens (4096 -> 14336 32.0 vs 37.9); 17..24
+//   and 9..16 tokens on weights of 64 M / 56 M+ elements (3584 -> 18944
+//   at M = 16 21.7 vs 23.9, 4096 -> 12288 stays on the weight ring, 21.7
+//   vs 22.9); up to 8 tokens only where the weight ring does not fit
+//   (8192 -> 18944: 51 us, no ring plan).
+static bool tc_decode_chosen(const LinearArgs& a) {
+  if (a.M > 32 || (a.fmt == 0 && a.group_size % 128 != 0)) return false;
+  const int64_t kn = (int64_t)a.K * a.N;
+  const bool tc_wins =
+      a.fmt == 1 ? (a.K >= 2048 || (a.M > 8 && a.M <= 16) || a.M > 24)
+                 : a.K >= 2048 && (a.M > 24 || (a.M > 16   ? kn >= ((int64_t)1 << 26)
+                                                : a.M > 8 ? kn >= ((int64_t)7 << 23)
+                                                          : kn >= ((int64_t)1 << 27)));
+  return tc_wins && decode_tc_rows(a) > 0;
+}
+
 static int linear_common(LinearArgs& a, cudaStream_t stream) {
   if (a.M == 0) return NSQ_OK;
   if (a.M <= kDecodeMaxM) {
@@ -292,26 +316,7 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     // and the Qwen2.5-0.5B shapes stay on the kernels below). AWQ group sizes
     // 32 and 64 run here for every M <= 32.
     const bool small_group = a.fmt == 0 && a.group_size % 128 != 0;
-    // Layers of 64-128 rows per SM: the tensor-core decode kernel (x as two
-    // narrow terms; FP8 A read from the TMA tile, AWQ A widened into tensor
-    // memory). Where it wins (B200, CUDA-graph chains of distinct weights,
-    // PDL; us, tensor core vs the best other kernel):
-    //   FP8, K >= 2048, every M: 4096 -> 14336 17.8 vs 20.7 (M = 1), 18.0 vs
-    //   23.7 (16), 23.4 vs 30.0 (32); 8192 -> 18944 32.5 vs 38.3 (1).
-    //   FP8, K < 2048 (896 -> 9472, 1024 -> 10000): within 0.5 us either way;
-    //   it takes 9..16 and 25..32 tokens.
-    //   AWQ, K >= 2048: 25..32 tokens (4096 -> 14336 32.0 vs 37.9); 17..24
-    //   and 9..16 tokens on weights of 64 M / 56 M+ elements (3584 -> 18944
-    //   at M = 16 21.7 vs 23.9, 4096 -> 12288 stays on the weight ring, 21.7
-    //   vs 22.9); up to 8 tokens only where the weight ring does not fit
-    //   (8192 -> 18944: 51 us, no ring plan).
-    const int64_t kn = (int64_t)a.K * a.N;
-    const bool tc_wins =
-        a.fmt == 1 ? (a.K >= 2048 || (a.M > 8 && a.M <= 16) || a.M > 24)
-                   : a.K >= 2048 && (a.M > 24 || (a.M > 16   ? kn >= ((int64_t)1 << 26)
-                                                  : a.M > 8 ? kn >= ((int64_t)7 << 23)
-                                                            : kn >= ((int64_t)1 << 27)));
-    if (a.M <= 32 && !small_group && tc_wins && decode_tc_rows(a) > 0) {
+    if (tc_decode_chosen(a)) {
       const int rc = run_decode_tc_linear(a, stream);
       if (rc != NSQ_ENOTSUP) return rc;
     }
@@ -353,12 +358,22 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
   return run_prefill_ts2_linear(a, stream);
 }
 
+size_t nsq_linear_workspace_size(int quant, int64_t M, int64_t K, int64_t N, int64_t group_size) {
+  if (M <= 0 || K <= 0 || N <= 0 || M > kIntMax || K > kIntMax || N > kIntMax || (quant != 0 && quant != 1)) return 0;
+  LinearArgs a{};
+  a.fmt = quant;
+  a.M = (int)M;
+  a.K = (int)K;
+  a.N = (int)N;
+  a.group_size = quant == 0 ? (int)group_size : 0;
+  if (quant == 0 && (group_size <= 0 || group_size > kIntMax)) return 0;
+  return tc_decode_chosen(a) ? decode_tc_workspace_bytes(a) : 0;
+}
+
 int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
                    const int32_t* qweight, const uint16_t* scales, const uint16_t* zeros,
                    int64_t group_size, const void* bias, int bias_dtype, void* y,
                    void* workspace, size_t workspace_bytes, void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (M < 0 || K <= 0 || N <= 0 || M > kIntMax || K > kIntMax || N > kIntMax) return NSQ_EINVAL;
   if (!valid_act_dtype(x_dtype) || !valid_bias_dtype(bias_dtype)) return NSQ_EINVAL;
   if ((bias_dtype == NSQ_DTYPE_NONE) != (bias == nullptr)) return NSQ_EINVAL;
@@ -384,6 +399,8 @@ int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
   a.bias = bias;
   a.bias_dtype = bias_dtype;
   a.y = y;
+  a.ws = workspace;
+  a.ws_bytes = workspace ? workspace_bytes : 0;
   return linear_common(a, static_cast<cudaStream_t>(stream));
 }
 
@@ -391,8 +408,6 @@ int nsq_fp8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
                    const uint8_t* weight_fp8, const float* weight_scale, const void* bias,
                    int bias_dtype, void* y, void* workspace, size_t workspace_bytes,
                    void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (M < 0 || K <= 0 || N <= 0 || M > kIntMax || K > kIntMax || N > kIntMax) return NSQ_EINVAL;
   if (!valid_act_dtype(x_dtype) || !valid_bias_dtype(bias_dtype)) return NSQ_EINVAL;
   if ((bias_dtype == NSQ_DTYPE_NONE) != (bias == nullptr)) return NSQ_EINVAL;
@@ -414,6 +429,8 @@ int nsq_fp8_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
   a.bias = bias;
   a.bias_dtype = bias_dtype;
   a.y = y;
+  a.ws = workspace;
+  a.ws_bytes = workspace ? workspace_bytes : 0;
   return linear_common(a, static_cast<cudaStream_t>(stream));
 }
 

@@ -68,9 +68,7 @@ constexpr int kTcWarpMma = 1;
 constexpr int kTcWarpPrep0 = 2;
 constexpr int kTcPrepWarps = 8;
 constexpr int kTcXGroups = 2;  // x-term groups of four warps, alternating k-blocks
-constexpr int kTcWarpEpi0 = kTcWarpPrep0 + kTcPrepWarps;
 constexpr int kTcEpiWarps = 4;
-constexpr int kTcWarpXfr0 = kTcWarpEpi0 + kTcEpiWarps;
 constexpr int kTcXfrWarps = 4;  // weight transfer: one per TMEM sub-partition
 constexpr int kTcND = 4;   // accumulators in TMEM
 constexpr int kTcNB = 4;   // x-term tiles
@@ -89,25 +87,33 @@ constexpr int kTcSmemMax = 227 * 1024;
 // k-blocks of packed nibbles. FP8: the UMMAs read A straight from the ring
 // slot (shared memory); AWQ: transfer warps widen it into tensor memory and
 // the UMMAs read A there.
-template <int FMT>
+// PRE: the x terms come precomputed (tc_xterm_kernel, once per launch instead
+// of once per CTA): one warp copies them in by TMA in place of the eight
+// x-term warps.
+template <int FMT, bool PRE>
 struct TcCfg {
   static constexpr bool kTmemA = FMT == 0;
-  static constexpr int kThreads = (kTmemA ? kTcWarpXfr0 + kTcXfrWarps : kTcWarpXfr0) * 32;
+  static constexpr int kEpi0 = PRE ? kTcWarpPrep0 + 1 : kTcWarpPrep0 + kTcPrepWarps;  // first epilogue warp
+  static constexpr int kXfr0 = kEpi0 + kTcEpiWarps;                                   // first transfer warp
+  static constexpr int kXfrGroups = 1;  // transfer groups of four warps taking alternate ring slots (two: no faster)
+  static constexpr int kThreads = (kTmemA ? kXfr0 + kXfrGroups * kTcXfrWarps : kXfr0) * 32;
   static constexpr int kKPS = FMT == 0 ? 2 : 1;  // k-blocks per ring slot
   static constexpr uint32_t kTmemCols = kTmemA ? 512 : 256;
 };
 
 // Fixed part of the shared-memory layout (after the weight ring, whose size
-// the plan chooses): x-term tiles, x k-blocks, per-token scalars, barriers.
-template <int MP>
+// the plan chooses): x-term tiles, x k-blocks (not with PRE), per-token
+// scalars, barriers.
+template <int MP, bool PRE>
 struct TcFixed {
   static constexpr int kBBytes = 2 * MP * 128;  // x-term tile: 2 MP rows (T1 rows, then T2 rows) x 128 B
   static constexpr int kXBytes = MP * 256;      // one x k-block: two boxes of [MP tokens x 64 columns] 16-bit
+  static constexpr int kNB = kTcNB;  // eight with precomputed terms measured no faster
   static constexpr int kB = 0;
-  static constexpr int kX = kB + kTcNB * kBBytes;
-  static constexpr int kXs = kX + kTcNXR * kXBytes;  // [NX][2][MP] fp32: scale 2^e, term sum (AWQ)
+  static constexpr int kX = kB + kNB * kBBytes;
+  static constexpr int kXs = kX + (PRE ? 0 : kTcNXR * kXBytes);  // [NX][2][MP] fp32: scale 2^e, term sum (AWQ)
   static constexpr int kBar = kXs + kTcNX * 2 * MP * 4;
-  static constexpr int kNumBars = 2 * kTcMaxNS + 2 * kTcNA + 2 * kTcNB + 2 * kTcND + 2 * kTcNX + kTcNXR + 1;
+  static constexpr int kNumBars = 2 * kTcMaxNS + 2 * kTcNA + 2 * kNB + 2 * kTcND + 2 * kTcNX + kTcNXR + 1;
   static constexpr int kTmemSlot = kBar + kNumBars * 8;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kBytes = ((kAbort + 4 + 1023) / 1024) * 1024;
@@ -130,6 +136,7 @@ struct TcParams {
   int tile;       // bytes of a ring slot: the tallest CTA's rows x 128 B
   int ns;         // weight ring slots (at shared-memory offset 0)
   int off_fixed;  // the fixed part (TcFixed)
+  const float* xsg;  // PRE: per-k-block scalars [nkb][2][MP] (the terms: tensor map bmap)
 };
 
 // Instruction descriptor: AWQ kind::i8 (A u8, B s8, D s32), FP8 kind::f8f6f4
@@ -233,6 +240,15 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// One contiguous global -> shared copy (no multicast), completing on `bar`;
+// both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // bytes 0 of a, b, c, d -> one word (a in the low byte)
 __device__ __forceinline__ uint32_t pack_b0(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return prmt(prmt(a, b, 0x5140u), prmt(c, d, 0x5140u), 0x5410u);
@@ -251,12 +267,91 @@ __device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t codes16) {
   return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
-template <int FMT, bool BF16, int MP>
-__global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(const __grid_constant__ CUtensorMap wmap_lo,
-                                                                             const __grid_constant__ CUtensorMap wmap_hi,
-                                                                             const __grid_constant__ CUtensorMap xmap,
-                                                                             const TcParams p) {
-  using F = TcFixed<MP>;
+// The x terms of one token's EPT columns of a k-block (this thread's share;
+// the token's TPT threads are adjacent lanes and reduce the block's largest
+// |x| and the term sums by shuffles): term bytes o1 (T1) and o2 (T2) in the A
+// operand's column order, the scale sc = 2^e and (AWQ) the term sum sx.
+template <int FMT, bool BF16, int EPT, int TPT>
+__device__ __forceinline__ void tc_x_terms(const uint4 (&v)[EPT / 8], uint32_t (&o1)[EPT / 4], uint32_t (&o2)[EPT / 4],
+                                           float& sc, float& sx) {
+  float f[EPT];
+#pragma unroll
+  for (int i = 0; i < EPT / 8; ++i) {
+    const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      f[8 * i + 2 * e] = elem_to_float<BF16>((uint16_t)(w[e] & 0xFFFFu));
+      f[8 * i + 2 * e + 1] = elem_to_float<BF16>((uint16_t)(w[e] >> 16));
+    }
+  }
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPT; ++i) mx = fmaxf(mx, fabsf(f[i]));
+#pragma unroll
+  for (int m = 1; m < TPT; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+  const int E = (__float_as_int(mx) >> 23) & 0xFF;  // biased exponent of the block's largest |x|
+  sc = 0.f;
+  sx = 0.f;
+  if constexpr (FMT == 0) {
+    // x * 2^-e in [-64, 64): e = E - 127 - 5; blocks below 2^-119 count as zero
+    const bool nz = E >= 12;
+    const float inv = nz ? __int_as_float((259 - E) << 23) : 0.f;
+    sc = nz ? __int_as_float((E - 5) << 23) : 0.f;
+    constexpr float kRnd = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer, kept in the low bits
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int g = 0; g < EPT / 8; ++g) {
+      uint32_t b1[8], b2[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float a1 = fmaf(f[8 * g + i], inv, kRnd);
+        const float t1 = a1 - kRnd;
+        const float rr = fmaf(f[8 * g + i], inv, -t1);
+        const float a2 = fmaf(rr, 128.0f, kRnd);
+        s1 += t1;
+        s2 += a2 - kRnd;
+        b1[i] = __float_as_uint(a1);  // low byte: the integer, two's complement
+        b2[i] = __float_as_uint(a2);
+      }
+      // widened weight bytes of one 32-bit word: columns 0,2,4,6 then 1,3,5,7
+      o1[2 * g] = pack_b0(b1[0], b1[2], b1[4], b1[6]);
+      o1[2 * g + 1] = pack_b0(b1[1], b1[3], b1[5], b1[7]);
+      o2[2 * g] = pack_b0(b2[0], b2[2], b2[4], b2[6]);
+      o2[2 * g + 1] = pack_b0(b2[1], b2[3], b2[5], b2[7]);
+    }
+#pragma unroll
+    for (int m = 1; m < TPT; m <<= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, m);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, m);
+    }
+    sx = s1 + s2 * 0.0078125f;
+  } else {
+    // x * 2^-e with its largest in [128, 256): e = E - 127 - 7; blocks below 2^-115 count as zero
+    const bool nz = E >= 12;
+    const float inv = nz ? __int_as_float((261 - E) << 23) : 0.f;
+    sc = nz ? __int_as_float((E - 7) << 23) : 0.f;
+#pragma unroll
+    for (int i = 0; i < EPT; i += 4) {
+      const float x0 = f[i] * inv, x1 = f[i + 1] * inv, x2 = f[i + 2] * inv, x3 = f[i + 3] * inv;
+      const uint32_t c01 = f32x2_to_e4m3x2(x1, x0), c23 = f32x2_to_e4m3x2(x3, x2);
+      const float2 v01 = e4m3x2_to_f32x2(c01), v23 = e4m3x2_to_f32x2(c23);
+      const uint32_t d01 = f32x2_to_e4m3x2((x1 - v01.y) * 16.0f, (x0 - v01.x) * 16.0f);
+      const uint32_t d23 = f32x2_to_e4m3x2((x3 - v23.y) * 16.0f, (x2 - v23.x) * 16.0f);
+      o1[i / 4] = c01 | (c23 << 16);
+      o2[i / 4] = d01 | (d23 << 16);
+    }
+  }
+  // an infinite or NaN x makes the token's outputs NaN, as the reference's
+  // matmul would (the terms of such a block are meaningless)
+  if (E == 255) sc = __int_as_float(0x7FC00000);
+}
+
+template <int FMT, bool BF16, int MP, bool PRE>
+__global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
+    decode_tc_kernel(const __grid_constant__ CUtensorMap wmap_lo, const __grid_constant__ CUtensorMap wmap_hi,
+                     const __grid_constant__ CUtensorMap xmap, const TcParams p) {
+  using F = TcFixed<MP, PRE>;
+  using C = TcCfg<FMT, PRE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* fx = smem + p.off_fixed;
@@ -273,8 +368,8 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
   uint64_t* afull = wempty + kTcMaxNS;
   uint64_t* aempty = afull + kTcNA;
   uint64_t* bfull = aempty + kTcNA;
-  uint64_t* bempty = bfull + kTcNB;
-  uint64_t* dfull = bempty + kTcNB;
+  uint64_t* bempty = bfull + F::kNB;
+  uint64_t* dfull = bempty + F::kNB;
   uint64_t* dempty = dfull + kTcND;
   uint64_t* xsfull = dempty + kTcND;
   uint64_t* xsempty = xsfull + kTcNX;
@@ -283,7 +378,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fx + F::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(fx + F::kAbort);
   float* xs = reinterpret_cast<float*>(fx + F::kXs);
-  constexpr int KPS = TcCfg<FMT>::kKPS;
+  constexpr int KPS = C::kKPS;
   const int NS = p.ns;
   const uint32_t tile = (uint32_t)p.tile;
 
@@ -300,13 +395,13 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     *abort_flag = 0;
     for (int i = 0; i < NS; ++i) {
       mbar_init(&wfull[i], 1);
-      mbar_init(&wempty[i], TcCfg<FMT>::kTmemA ? kTcXfrWarps : 1);
+      mbar_init(&wempty[i], C::kTmemA ? kTcXfrWarps : 1);
     }
     for (int i = 0; i < kTcNA; ++i) {
       mbar_init(&afull[i], kTcXfrWarps);
       mbar_init(&aempty[i], 1);
     }
-    for (int i = 0; i < kTcNB; ++i) {
+    for (int i = 0; i < F::kNB; ++i) {
       mbar_init(&bfull[i], 1);
       mbar_init(&bempty[i], 1);
     }
@@ -323,7 +418,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     fence_barrier_init();
   }
   if (warp == kTcWarpMma) {
-    tmem_alloc(tmem_slot, TcCfg<FMT>::kTmemCols);
+    tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -357,12 +452,12 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     // ---------------- UMMA issuer (whole warp, converged) ----------------
     const uint32_t idesc = tc_idesc(FMT, kTcM, 2 * MP);
     for (int b = 0; b < nkb; ++b) {
-      const int s = b % kTcNB, d = b % kTcND;  // x-term tile, accumulator
+      const int s = b % F::kNB, d = b % kTcND;  // x-term tile, accumulator
       // the A tile: FP8 ring slot b % ns; AWQ tensor-memory tile b % kTcNA
       const int a = FMT == 1 ? b % NS : b % kTcNA;
       uint64_t* abar = FMT == 1 ? &wfull[a] : &afull[a];
       const uint32_t apar = FMT == 1 ? ((b / NS) & 1) : ((b / kTcNA) & 1);
-      const uint32_t bpar = (b / kTcNB) & 1;
+      const uint32_t bpar = (b / F::kNB) & 1;
       const uint32_t dpar = ((b / kTcND) - 1) & 1;  // accumulator d free again (k-block b - kTcND read out)
       // the A tile, the x-term tile and the accumulator
       const bool ready = __all_sync(
@@ -387,7 +482,32 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     // every UMMA issued has finished before TMEM is released
     tc_commit_elect(mdone);
     mbar_wait(mdone, 0, nullptr, 0, nullptr);
-  } else if (warp < kTcWarpEpi0) {
+  } else if (warp < C::kEpi0 && PRE) {
+    // ---------------- x terms by TMA (precomputed) ----------------
+    // xmap covers the terms [nkb x 2 MP rows][128 B]: one box of a k-block's
+    // 2 MP rows lands as the x-term tile (128-byte swizzle); its scalars
+    // [2][MP] fp32 follow by one bulk copy.
+    if (lane == 0) {
+      tma_prefetch_desc(&xmap);
+      pdl_wait_prior_grids();  // the terms are written by the previous kernel
+      int b = 0;
+      for (; b < nkb; ++b) {
+        const int s = b % F::kNB, xsl = b % kTcNX;
+        if (b >= F::kNB && !(ok = mbar_wait(&bempty[s], ((b / F::kNB) - 1) & 1, p.status, 85, abort_flag))) break;
+        if (b >= kTcNX && !(ok = mbar_wait(&xsempty[xsl], ((b / kTcNX) - 1) & 1, p.status, 86, abort_flag))) break;
+        mbar_arrive_expect_tx(&bfull[s], (uint32_t)F::kBBytes);
+        tma_load_2d(fx + F::kB + s * F::kBBytes, &xmap, &bfull[s], 0, b * 2 * MP);
+        mbar_arrive_expect_tx(&xsfull[xsl], (uint32_t)(2 * MP * 4));
+        bulk_load_1d(xs + xsl * 2 * MP, p.xsg + (size_t)b * 2 * MP, 2 * MP * 4, &xsfull[xsl]);
+      }
+      if (!ok) {  // copies in flight land before the CTA can exit
+        for (int j = (b > F::kNB ? b - F::kNB : 0); j < b; ++j)
+          mbar_wait(&bfull[j % F::kNB], (j / F::kNB) & 1, nullptr, 0, nullptr);
+        for (int j = (b > kTcNX ? b - kTcNX : 0); j < b; ++j)
+          mbar_wait(&xsfull[j % kTcNX], (j / kTcNX) & 1, nullptr, 0, nullptr);
+      }
+    }
+  } else if (warp < C::kEpi0) {
     // ---------------- x terms ----------------
     pdl_wait_prior_grids();  // x is written by the previous kernel
     constexpr int kGT = kTcPrepWarps / kTcXGroups * 32;  // threads of a group
@@ -414,13 +534,13 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     const int xc0 = part * EPT;  // first column of this thread within the k-block
     const uint32_t xsrc0 = (uint32_t)((xc0 >> 6) * (F::kXBytes / 2) + tok * 128 + (xc0 & 63) * 2);
     for (int b = grp; b < nkb; b += kTcXGroups) {
-      const int s = b % kTcNB, xsl = b % kTcNX, xr = b % kTcNXR;
+      const int s = b % F::kNB, xsl = b % kTcNX, xr = b % kTcNXR;
       const uint32_t xpar = (b / kTcNXR) & 1;
       // the x-term tile and the scalar slot free, the x k-block landed
-      if (!mbar_test3(b >= kTcNB ? &bempty[s] : &xfull[xr], b >= kTcNB ? (((b / kTcNB) - 1) & 1) : xpar,
+      if (!mbar_test3(b >= F::kNB ? &bempty[s] : &xfull[xr], b >= F::kNB ? (((b / F::kNB) - 1) & 1) : xpar,
                       b >= kTcNX ? &xsempty[xsl] : &xfull[xr], b >= kTcNX ? (((b / kTcNX) - 1) & 1) : xpar, &xfull[xr],
                       xpar)) {
-        if (b >= kTcNB && !(ok = mbar_wait(&bempty[s], ((b / kTcNB) - 1) & 1, p.status, 85, abort_flag))) break;
+        if (b >= F::kNB && !(ok = mbar_wait(&bempty[s], ((b / F::kNB) - 1) & 1, p.status, 85, abort_flag))) break;
         if (b >= kTcNX && !(ok = mbar_wait(&xsempty[xsl], ((b / kTcNX) - 1) & 1, p.status, 86, abort_flag))) break;
         if (!(ok = mbar_wait(&xfull[xr], xpar, p.status, 91, abort_flag))) break;
       }
@@ -428,76 +548,9 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
       uint4 v[EPT / 8];
 #pragma unroll
       for (int i = 0; i < EPT / 8; ++i) v[i] = lds128(xsrc + 16 * i);
-      float f[EPT];
-#pragma unroll
-      for (int i = 0; i < EPT / 8; ++i) {
-        const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          f[8 * i + 2 * e] = elem_to_float<BF16>((uint16_t)(w[e] & 0xFFFFu));
-          f[8 * i + 2 * e + 1] = elem_to_float<BF16>((uint16_t)(w[e] >> 16));
-        }
-      }
-      float mx = 0.f;
-#pragma unroll
-      for (int i = 0; i < EPT; ++i) mx = fmaxf(mx, fabsf(f[i]));
-#pragma unroll
-      for (int m = 1; m < TPT; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-      const int E = (__float_as_int(mx) >> 23) & 0xFF;  // biased exponent of the block's largest |x|
-      uint32_t o1[EPT / 4], o2[EPT / 4];                 // term bytes, in the A operand's column order
-      float sc = 0.f, sx = 0.f;
-      if constexpr (FMT == 0) {
-        // x * 2^-e in [-64, 64): e = E - 127 - 5; blocks below 2^-119 count as zero
-        const bool nz = E >= 12;
-        const float inv = nz ? __int_as_float((259 - E) << 23) : 0.f;
-        sc = nz ? __int_as_float((E - 5) << 23) : 0.f;
-        constexpr float kRnd = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer, kept in the low bits
-        float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-        for (int g = 0; g < EPT / 8; ++g) {
-          uint32_t b1[8], b2[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float a1 = fmaf(f[8 * g + i], inv, kRnd);
-            const float t1 = a1 - kRnd;
-            const float rr = fmaf(f[8 * g + i], inv, -t1);
-            const float a2 = fmaf(rr, 128.0f, kRnd);
-            s1 += t1;
-            s2 += a2 - kRnd;
-            b1[i] = __float_as_uint(a1);  // low byte: the integer, two's complement
-            b2[i] = __float_as_uint(a2);
-          }
-          // widened weight bytes of one 32-bit word: columns 0,2,4,6 then 1,3,5,7
-          o1[2 * g] = pack_b0(b1[0], b1[2], b1[4], b1[6]);
-          o1[2 * g + 1] = pack_b0(b1[1], b1[3], b1[5], b1[7]);
-          o2[2 * g] = pack_b0(b2[0], b2[2], b2[4], b2[6]);
-          o2[2 * g + 1] = pack_b0(b2[1], b2[3], b2[5], b2[7]);
-        }
-#pragma unroll
-        for (int m = 1; m < TPT; m <<= 1) {
-          s1 += __shfl_xor_sync(0xffffffffu, s1, m);
-          s2 += __shfl_xor_sync(0xffffffffu, s2, m);
-        }
-        sx = s1 + s2 * 0.0078125f;
-      } else {
-        // x * 2^-e with its largest in [128, 256): e = E - 127 - 7; blocks below 2^-115 count as zero
-        const bool nz = E >= 12;
-        const float inv = nz ? __int_as_float((261 - E) << 23) : 0.f;
-        sc = nz ? __int_as_float((E - 7) << 23) : 0.f;
-#pragma unroll
-        for (int i = 0; i < EPT; i += 4) {
-          const float x0 = f[i] * inv, x1 = f[i + 1] * inv, x2 = f[i + 2] * inv, x3 = f[i + 3] * inv;
-          const uint32_t c01 = f32x2_to_e4m3x2(x1, x0), c23 = f32x2_to_e4m3x2(x3, x2);
-          const float2 v01 = e4m3x2_to_f32x2(c01), v23 = e4m3x2_to_f32x2(c23);
-          const uint32_t d01 = f32x2_to_e4m3x2((x1 - v01.y) * 16.0f, (x0 - v01.x) * 16.0f);
-          const uint32_t d23 = f32x2_to_e4m3x2((x3 - v23.y) * 16.0f, (x2 - v23.x) * 16.0f);
-          o1[i / 4] = c01 | (c23 << 16);
-          o2[i / 4] = d01 | (d23 << 16);
-        }
-      }
-      // an infinite or NaN x makes the token's outputs NaN, as the reference's
-      // matmul would (the terms of such a block are meaningless)
-      if (E == 255) sc = __int_as_float(0x7FC00000);
+      uint32_t o1[EPT / 4], o2[EPT / 4];  // term bytes, in the A operand's column order
+      float sc, sx;
+      tc_x_terms<FMT, BF16, EPT, TPT>(v, o1, o2, sc, sx);
       // term rows tok (T1) and MP + tok (T2) of the x-term tile
       const uint32_t bt = smem_u32(fx + F::kB + s * F::kBBytes);
 #pragma unroll
@@ -531,7 +584,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
         mbar_wait(&xfull[bb % kTcNXR], (bb / kTcNXR) & 1, nullptr, 0, nullptr);
       }
     }
-  } else if (warp < kTcWarpXfr0) {
+  } else if (warp < C::kXfr0) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;  // TMEM sub-partition: rows 32 q .. 32 q + 31
     const int row = q * 32 + lane;
@@ -543,19 +596,23 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     for (int i = 0; i < MP; ++i) acc[i] = 0.f;
     const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
     const unsigned short* zr16 = reinterpret_cast<const unsigned short*>(p.zeros);
-    // AWQ: (scale, zero point) of this row for the next k-block, loaded one block ahead
+    // AWQ: (scale, zero point) of this row for k-block b (0 past K or for rows past N)
     auto load_sz = [&](int b) -> uint32_t {
       if (FMT != 0 || !rv || b >= nkb) return 0u;
       const int64_t off = (int64_t)n * p.G + (b * 128) / p.group_size;
       return (uint32_t)__ldg(sc16 + off) | ((uint32_t)__ldg(zr16 + off) << 16);
     };
-    uint32_t sz_next = load_sz(0);
+    // four k-blocks ahead (a global load's latency is about two k-blocks' time)
+    uint32_t sz0 = load_sz(0), sz1 = load_sz(1), sz2 = load_sz(2), sz3 = load_sz(3);
     for (int b = 0; b < nkb; ++b) {
       const int d = b % kTcND, xsl = b % kTcNX;
-      const uint32_t sz = sz_next;
-      sz_next = load_sz(b + 1);
-      if (!(ok = mbar_wait(&dfull[d], (b / kTcND) & 1, p.status, 87, abort_flag))) break;
-      if (!(ok = mbar_wait(&xsfull[xsl], (b / kTcNX) & 1, p.status, 88, abort_flag))) break;
+      const uint32_t sz = sz0;
+      sz0 = sz1, sz1 = sz2, sz2 = sz3, sz3 = load_sz(b + 4);
+      // the accumulator and the k-block's scalars
+      if (!mbar_test3(&dfull[d], (b / kTcND) & 1, &xsfull[xsl], (b / kTcNX) & 1, &xsfull[xsl], (b / kTcNX) & 1)) {
+        if (!(ok = mbar_wait(&dfull[d], (b / kTcND) & 1, p.status, 87, abort_flag))) break;
+        if (!(ok = mbar_wait(&xsfull[xsl], (b / kTcNX) & 1, p.status, 88, abort_flag))) break;
+      }
       tc_fence_after();
       const float s = __half2float(__ushort_as_half((unsigned short)(sz & 0xFFFFu)));
       const float z = __half2float(__ushort_as_half((unsigned short)(sz >> 16)));
@@ -597,7 +654,7 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
         }
       }
     }
-  } else if constexpr (TcCfg<FMT>::kTmemA) {
+  } else if constexpr (C::kTmemA) {
     // ---------------- AWQ weight transfer: ring slot -> tensor-memory A tiles ----------------
     // Lane i of warp w holds weight row 32 (w % 4) + i (its TMEM lane). A ring
     // slot is two k-blocks; the row's 128 bytes are 16-byte chunks c at
@@ -608,12 +665,16 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
     // terms are packed in. Rows past the CTA's store zeros (their accumulator
     // lanes are never read). Per slot: all loads, both k-blocks' stores, one
     // tcgen05.wait::st.
+    // With two groups, group g takes ring slots g, g + 2, ... (k-blocks 4i + 2g
+    // and 4i + 2g + 1: A tiles 2g and 2g + 1).
     const int q = warp & 3;
+    static_assert(C::kXfrGroups == 1 || (kTcNA == 4 && KPS == 2), "two groups: A tiles 0-1 and 2-3");
+    const int grp = (warp - C::kXfr0) / kTcXfrWarps;
     const int row = q * 32 + lane;
     const bool rin = row < rows;
     const uint32_t tl = tmem_base + ((uint32_t)(q * 32) << 16);  // this warp's 32 lanes
     const int nst = (nkb + KPS - 1) / KPS;
-    for (int st = 0; st < nst && ok; ++st) {
+    for (int st = grp; st < nst && ok; st += C::kXfrGroups) {
       const int rs = st % NS, b0 = KPS * st, nb = min(KPS, nkb - b0);
       const uint32_t wpar = (st / NS) & 1;
       if (!__all_sync(0xffffffffu, mbar_test1(&wfull[rs], wpar))) {
@@ -667,14 +728,66 @@ __global__ void __launch_bounds__(TcCfg<FMT>::kThreads, 1) decode_tc_kernel(cons
   __syncthreads();
   if (warp == kTcWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TcCfg<FMT>::kTmemCols);
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// The x terms of one launch, once (one CTA per k-block, 128 threads, the
+// token's 128 / MP threads adjacent): the x-term tile of k-block b as rows
+// [b * 2 MP, b * 2 MP + 2 MP) of 128 bytes (T1 rows of the MP token slots,
+// then their T2 rows; unswizzled, the tensor map swizzles on the way in) and
+// its scalars xsg[b][0][tok] = 2^e, xsg[b][1][tok] = term sum (AWQ). Token
+// slots past M get zero terms.
+template <int FMT, bool BF16, int MP>
+__global__ void __launch_bounds__(128) tc_xterm_kernel(const void* x, int M, int K, uint8_t* xt, float* xsg) {
+  pdl_launch_dependents();
+  pdl_wait_prior_grids();  // x is written by the previous kernel
+  constexpr int TPT = 128 / MP, EPT = 128 / TPT;
+  const int b = (int)blockIdx.x, t = (int)threadIdx.x;
+  const int tok = t / TPT, part = t - (t / TPT) * TPT;
+  uint4 v[EPT / 8];
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + (int64_t)tok * K + b * 128 +
+                                                    part * EPT);
+#pragma unroll
+  for (int i = 0; i < EPT / 8; ++i) v[i] = tok < M ? __ldg(src + i) : make_uint4(0u, 0u, 0u, 0u);
+  uint32_t o1[EPT / 4], o2[EPT / 4];
+  float sc, sx;
+  tc_x_terms<FMT, BF16, EPT, TPT>(v, o1, o2, sc, sx);
+  uint4* rows = reinterpret_cast<uint4*>(xt + (int64_t)b * 2 * MP * 128);
+#pragma unroll
+  for (int cc = 0; cc < EPT / 16; ++cc) {
+    const int chunk = part * (EPT / 16) + cc;
+    rows[tok * 8 + chunk] = make_uint4(o1[4 * cc], o1[4 * cc + 1], o1[4 * cc + 2], o1[4 * cc + 3]);
+    rows[(MP + tok) * 8 + chunk] = make_uint4(o2[4 * cc], o2[4 * cc + 1], o2[4 * cc + 2], o2[4 * cc + 3]);
+  }
+  if (part == 0) {
+    xsg[(int64_t)b * 2 * MP + tok] = sc;
+    xsg[(int64_t)b * 2 * MP + MP + tok] = sx;
   }
 }
 
 template <int FMT, bool BF16, int MP>
+cudaError_t launch_xterm(const void* x, int M, int K, uint8_t* xt, float* xsg, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(K / 128, 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    na = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, tc_xterm_kernel<FMT, BF16, MP>, x, M, K, xt, xsg);
+}
+
+template <int FMT, bool BF16, int MP, bool PRE>
 cudaError_t launch_tc(const CUtensorMap& wlo, const CUtensorMap& whi, const CUtensorMap& xmap, const TcParams& p,
                       int grid, cudaStream_t stream) {
-  auto kern = decode_tc_kernel<FMT, BF16, MP>;
+  auto kern = decode_tc_kernel<FMT, BF16, MP, PRE>;
   static std::atomic<bool> configured{false};
   if (!configured.load()) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
@@ -683,8 +796,8 @@ cudaError_t launch_tc(const CUtensorMap& wlo, const CUtensorMap& whi, const CUte
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(TcCfg<FMT>::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = (size_t)p.off_fixed + TcFixed<MP>::kBytes + 1024;
+  cfg.blockDim = dim3(TcCfg<FMT, PRE>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)p.off_fixed + TcFixed<MP, PRE>::kBytes + 1024;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   int na = 0;
@@ -699,10 +812,17 @@ cudaError_t launch_tc(const CUtensorMap& wlo, const CUtensorMap& whi, const CUte
 }
 
 template <int FMT, bool BF16>
-cudaError_t dispatch_tc(int mp, const CUtensorMap& wlo, const CUtensorMap& whi, const CUtensorMap& xmap,
-                        const TcParams& p, int grid, cudaStream_t s) {
-  return mp == 16 ? launch_tc<FMT, BF16, 16>(wlo, whi, xmap, p, grid, s)
-                  : launch_tc<FMT, BF16, 32>(wlo, whi, xmap, p, grid, s);
+cudaError_t dispatch_tc(int mp, bool pre, const CUtensorMap& wlo, const CUtensorMap& whi, const CUtensorMap& xmap,
+                        const TcParams& p, int grid, const void* x, uint8_t* xt, cudaStream_t s) {
+  if (pre) {
+    cudaError_t e = mp == 16 ? launch_xterm<FMT, BF16, 16>(x, p.M, p.K, xt, const_cast<float*>(p.xsg), s)
+                             : launch_xterm<FMT, BF16, 32>(x, p.M, p.K, xt, const_cast<float*>(p.xsg), s);
+    if (e != cudaSuccess) return e;
+    return mp == 16 ? launch_tc<FMT, BF16, 16, true>(wlo, whi, xmap, p, grid, s)
+                    : launch_tc<FMT, BF16, 32, true>(wlo, whi, xmap, p, grid, s);
+  }
+  return mp == 16 ? launch_tc<FMT, BF16, 16, false>(wlo, whi, xmap, p, grid, s)
+                  : launch_tc<FMT, BF16, 32, false>(wlo, whi, xmap, p, grid, s);
 }
 
 }  // namespace
@@ -731,11 +851,20 @@ int decode_tc_rows(const LinearArgs& a) {
   return rlo + (nhi > 0 ? 8 : 0);
 }
 
+size_t decode_tc_workspace_bytes(const LinearArgs& a) {
+  const int64_t nkb = a.K / 128, rows = nkb * 2 * (a.M <= 16 ? 16 : 32);
+  return (size_t)(rows * 128 + rows * 4);
+}
+
 int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
   int rlo, nhi, grid;
   if (!tc_rows(a, &rlo, &nhi, &grid)) return NSQ_ENOTSUP;
   const int rmax = rlo + (nhi > 0 ? 8 : 0);
   const int mp = a.M <= 16 ? 16 : 32;
+  // with a workspace, the x terms are computed once by tc_xterm_kernel: the
+  // terms [nkb x 2 mp rows][128 B], then the scalars [nkb][2][mp] fp32
+  const bool pre = a.ws != nullptr && a.ws_bytes >= decode_tc_workspace_bytes(a) && ((uintptr_t)a.ws & 15) == 0;
+  uint8_t* xt = static_cast<uint8_t*>(a.ws);
   TcParams p{};
   p.x = a.x;
   p.scales = reinterpret_cast<const __half*>(a.scales);
@@ -756,7 +885,8 @@ int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
   // Shared memory: the weight ring (sized to what is left, at most kTcMaxNS
   // slots of the tallest CTA's rows x 128 B), then the fixed part.
   p.tile = rmax * 128;
-  const int fixed = mp == 16 ? TcFixed<16>::kBytes : TcFixed<32>::kBytes;
+  const int fixed = pre ? (mp == 16 ? TcFixed<16, true>::kBytes : TcFixed<32, true>::kBytes)
+                        : (mp == 16 ? TcFixed<16, false>::kBytes : TcFixed<32, false>::kBytes);
   const int room = kTcSmemMax - 1024 - fixed;
   p.ns = room / p.tile;
   if (p.ns > kTcMaxNS) p.ns = kTcMaxNS;
@@ -772,20 +902,29 @@ int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
   cr = encode_tensor_map_2d(&wmap_hi, CU_TENSOR_MAP_DATA_TYPE_INT32, const_cast<void*>(a.wq), row_bytes / 4,
                             (uint64_t)a.N, row_bytes, 32, (uint32_t)rmax, CU_TENSOR_MAP_SWIZZLE_128B);
   if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
-  // x, rank 3: [64-column halves of a k-block][tokens][64 columns] 16-bit, one
-  // box of [2][mp][64] per k-block (tokens past M read as zero)
   CUtensorMap xmap;
-  cr = encode_tensor_map_3d(&xmap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                            const_cast<void*>(a.x), 64, (uint64_t)a.M, (uint64_t)a.K / 64, (uint64_t)a.K * 2, 128, 64,
-                            (uint32_t)mp, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (pre) {
+    // the precomputed terms as 32-bit words [nkb * 2 mp rows x 32 words], one
+    // box of [2 mp rows x 128 B] per k-block, 128-byte swizzle
+    const uint64_t trows = (uint64_t)p.nkb * 2 * mp;
+    p.xsg = reinterpret_cast<const float*>(xt + trows * 128);
+    cr = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_INT32, xt, 32, trows, 128, 32, (uint32_t)(2 * mp),
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    // x, rank 3: [64-column halves of a k-block][tokens][64 columns] 16-bit,
+    // one box of [2][mp][64] per k-block (tokens past M read as zero)
+    cr = encode_tensor_map_3d(&xmap, a.x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              const_cast<void*>(a.x), 64, (uint64_t)a.M, (uint64_t)a.K / 64, (uint64_t)a.K * 2, 128,
+                              64, (uint32_t)mp, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
   if (cr != CUDA_SUCCESS) return NSQ_ECUDA;
   cudaError_t e;
   if (a.fmt == 0) {
-    e = a.x_bf16 ? dispatch_tc<0, true>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream)
-                 : dispatch_tc<0, false>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream);
+    e = a.x_bf16 ? dispatch_tc<0, true>(mp, pre, wmap_lo, wmap_hi, xmap, p, grid, a.x, xt, stream)
+                 : dispatch_tc<0, false>(mp, pre, wmap_lo, wmap_hi, xmap, p, grid, a.x, xt, stream);
   } else {
-    e = a.x_bf16 ? dispatch_tc<1, true>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream)
-                 : dispatch_tc<1, false>(mp, wmap_lo, wmap_hi, xmap, p, grid, stream);
+    e = a.x_bf16 ? dispatch_tc<1, true>(mp, pre, wmap_lo, wmap_hi, xmap, p, grid, a.x, xt, stream)
+                 : dispatch_tc<1, false>(mp, pre, wmap_lo, wmap_hi, xmap, p, grid, a.x, xt, stream);
   }
   return e == cudaSuccess ? NSQ_OK : NSQ_ECUDA;
 }

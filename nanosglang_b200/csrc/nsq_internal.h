@@ -56,6 +56,8 @@ struct LinearArgs {
   const void* bias;
   int bias_dtype;
   void* y;
+  void* ws;  // caller workspace (may be null)
+  size_t ws_bytes;
 };
 int run_decode_wave_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 64, one wave of CTAs
 int run_decode_stream_linear(const LinearArgs& a, cudaStream_t stream);  // M <= 64, persistent weight ring
@@ -91,6 +93,9 @@ int run_decode_rows_linear(const LinearArgs& a, cudaStream_t stream);
 // Tensor-core decode kernel (M <= 32, K % 128 == 0, AWQ groups of 128 k, 64 to
 // 128 weight rows per SM): rows per CTA, or 0 if it does not apply.
 int decode_tc_rows(const LinearArgs& a);
+// Workspace with which the kernel takes precomputed x terms (one small kernel
+// ahead of it instead of every CTA computing them); without it, the CTAs do.
+size_t decode_tc_workspace_bytes(const LinearArgs& a);
 int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream);
 // prefill: the weight tile dequantised into tensor memory (A operand), tokens
 // as UMMA N. One CTA per 128 weight rows x 64/128 tokens, K optionally split

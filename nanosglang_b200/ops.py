@@ -87,6 +87,20 @@ def awq_dequant(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor
     return out
 
 
+def _decode_workspace(lib, quant: int, m: int, k: int, n: int, group_size: int, device):
+    """(tensor, bytes) of a workspace for the decode batch sizes whose kernel
+    runs faster with one (x converted once per call, ahead of the linear),
+    else (None, 0). The tensor comes from the caching allocator on the
+    current stream, so its reuse is stream-ordered after the launches that
+    read it (also under CUDA-graph capture)."""
+    if m > 32:
+        return None, 0
+    nbytes = lib.nsq_linear_workspace_size(quant, m, k, n, group_size)
+    if not nbytes:
+        return None, 0
+    return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+
+
 def awq_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor,
                group_size: int, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """``AWQLinear.forward`` (quantization.py:150-152) on the tensor cores.
@@ -120,8 +134,11 @@ def awq_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zer
     else:
         b, bcode = _bias_arg(bias)
         bptr = b.data_ptr()
-    rc = _lib.load().nsq_awq_linear(x2.data_ptr(), code, m, k, n, qweight.data_ptr(), scales.data_ptr(),
-                                    zeros.data_ptr(), group_size, bptr, bcode, y.data_ptr(), None, 0, _stream(x))
+    lib = _lib.load()
+    ws, wsb = _decode_workspace(lib, 0, m, k, n, group_size, x.device)
+    rc = lib.nsq_awq_linear(x2.data_ptr(), code, m, k, n, qweight.data_ptr(), scales.data_ptr(),
+                            zeros.data_ptr(), group_size, bptr, bcode, y.data_ptr(),
+                            None if ws is None else ws.data_ptr(), wsb, _stream(x))
     if rc:
         _lib.check(rc, "nsq_awq_linear")
     return y if x.dim() == 2 else y.reshape(*x.shape[:-1], n)
@@ -229,8 +246,10 @@ def fp8_linear(x: torch.Tensor, weight_fp8: torch.Tensor, weight_scale: torch.Te
     s = weight_scale
     if s.dtype != torch.float32 or s.numel() != 1 or not s.is_contiguous():
         s = _scale_arg(s)
-    rc = _lib.load().nsq_fp8_linear(x2.data_ptr(), code, m, k, n, w.data_ptr(), s.data_ptr(), bptr, bcode,
-                                    y.data_ptr(), None, 0, _stream(x))
+    lib = _lib.load()
+    ws, wsb = _decode_workspace(lib, 1, m, k, n, 0, x.device)
+    rc = lib.nsq_fp8_linear(x2.data_ptr(), code, m, k, n, w.data_ptr(), s.data_ptr(), bptr, bcode,
+                            y.data_ptr(), None if ws is None else ws.data_ptr(), wsb, _stream(x))
     if rc:
         _lib.check(rc, "nsq_fp8_linear")
     return y if x.dim() == 2 else y.reshape(*x.shape[:-1], n)

@@ -373,6 +373,41 @@ def test_tensor_core_decode_nonfinite_x(fmt):
     assert O.rel_fro(yn[keep], ref[keep]) <= GEMM_TOL
 
 
+@pytest.mark.parametrize("fmt", ["fp8", "awq"])
+@pytest.mark.parametrize("m", [16, 32])
+def test_tensor_core_decode_workspace_and_without(fmt, m):
+    """The C ABI with and without the workspace nsq_linear_workspace_size asks for: with it the x terms are
+    computed once by a kernel ahead of the linear, without it by every CTA; both match the oracle."""
+    from nanosglang_b200 import _lib
+    lib = _lib.load()
+    n, k = 14336, 4096
+    assert lib.nsq_linear_workspace_size(1 if fmt == "fp8" else 0, m, k, n, 128) == (k // 128) * 2 * m * 132
+    assert lib.nsq_linear_workspace_size(1 if fmt == "fp8" else 0, m, 896, 896, 128) == 0  # not a tensor-core shape
+    x = rand_x(m, k, torch.bfloat16, 61).cuda()
+    y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    if fmt == "fp8":
+        rng = np.random.default_rng(62)
+        codes, scale = O.fp8_quantize((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+        cw, sw = torch.from_numpy(codes).cuda(), torch.tensor(scale).cuda()
+        ref = O.fp8_linear(_to_np(x.cpu()), codes, scale)
+        call = lambda ws, nb: lib.nsq_fp8_linear(x.data_ptr(), _lib.DTYPE_BF16, m, k, n, cw.data_ptr(), sw.data_ptr(),
+                                                 None, _lib.DTYPE_NONE, y.data_ptr(), ws, nb, stream)
+    else:
+        (qw, s, z), (tq, ts, tz) = rand_awq(n, k, 128, seed=63, zero_mode="int")
+        ref = O.awq_linear(_to_np(x.cpu()), qw, s, z, k, 128)
+        call = lambda ws, nb: lib.nsq_awq_linear(x.data_ptr(), _lib.DTYPE_BF16, m, k, n, tq.data_ptr(), ts.data_ptr(),
+                                                 tz.data_ptr(), 128, None, _lib.DTYPE_NONE, y.data_ptr(), ws, nb,
+                                                 stream)
+    nb = lib.nsq_linear_workspace_size(1 if fmt == "fp8" else 0, m, k, n, 128)
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    for wsp, wsb in [(ws.data_ptr(), nb), (None, 0), (ws.data_ptr(), nb - 16)]:  # too small a workspace is ignored
+        y.fill_(float("nan"))
+        assert call(wsp, wsb) == 0
+        torch.cuda.synchronize()
+        assert O.rel_fro(_to_np(y), ref) <= GEMM_TOL
+
+
 def test_fp8_linear_tensor_core_decode_wide_range_x():
     """x spanning many binades within a k-block (per-token, per-k-block power-of-two scales of the terms)."""
     from nanosglang_b200 import ops
