@@ -278,11 +278,17 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
 //   at M = 16 21.7 vs 23.9, 4096 -> 12288 stays on the weight ring, 21.7
 //   vs 22.9); up to 8 tokens only where the weight ring does not fit
 //   (8192 -> 18944: 51 us, no ring plan).
+//   33..64 tokens (with a workspace), K >= 2048: AWQ 4096 -> 14336 at M = 64
+//   40.9 vs 47.3 (the one-CTA prefill kernel), 8192 -> 18944 76.4 vs 92.3;
+//   FP8 4096 -> 14336 24.6 vs 25.8, 8192 -> 18944 40.5 vs 47.0; FP8 below
+//   32 M weight elements (2048 -> 10000) is a tie and stays.
 static bool tc_decode_chosen(const LinearArgs& a) {
-  if (a.M > 32 || (a.fmt == 0 && a.group_size % 128 != 0)) return false;
+  if (a.M > 64 || (a.fmt == 0 && a.group_size % 128 != 0)) return false;
   const int64_t kn = (int64_t)a.K * a.N;
+  // 33..64 tokens run only with precomputed x terms (a workspace)
   const bool tc_wins =
-      a.fmt == 1 ? (a.K >= 2048 || (a.M > 8 && a.M <= 16) || a.M > 24)
+      a.M > 32 ? a.K >= 2048 && (a.fmt == 0 || kn >= ((int64_t)1 << 25))
+      : a.fmt == 1 ? (a.K >= 2048 || (a.M > 8 && a.M <= 16) || a.M > 24)
                  : a.K >= 2048 && (a.M > 24 || (a.M > 16   ? kn >= ((int64_t)1 << 26)
                                                 : a.M > 8 ? kn >= ((int64_t)7 << 23)
                                                           : kn >= ((int64_t)1 << 27)));
@@ -305,6 +311,10 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     // work grows with the token count (B200, CUDA-graph chains, AWQ at
     // M = 64: Llama-3-8B gate 140 -> 47 us, down 146 -> 47 us, q 52 -> 18 us,
     // 896 -> 9728 19.5 -> 12.6 us; 4096 -> 1024 stays faster on mma.sync)
+    if (tc_decode_chosen(a)) {
+      const int rc = run_decode_tc_linear(a, stream);
+      if (rc != NSQ_ENOTSUP) return rc;
+    }
     if (a.M > 32 && (int64_t)a.K * a.N >= ((int64_t)1 << 23)) {
       const TsPlan tp = prefill_ts_plan(a.fmt, a.M, a.K, a.N);
       if (tp.tokens_per_tile > 0) return run_prefill_ts_linear(a, tp, stream);
@@ -316,10 +326,6 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     // and the Qwen2.5-0.5B shapes stay on the kernels below). AWQ group sizes
     // 32 and 64 run here for every M <= 32.
     const bool small_group = a.fmt == 0 && a.group_size % 128 != 0;
-    if (tc_decode_chosen(a)) {
-      const int rc = run_decode_tc_linear(a, stream);
-      if (rc != NSQ_ENOTSUP) return rc;
-    }
     if (a.M <= 32 && (small_group ||((int64_t)a.K * a.N >= ((int64_t)1 << 24) && (a.fmt == 1 || a.M > 16)))) {
       const int rc = run_decode_rows_linear(a, stream);
       if (rc != NSQ_ENOTSUP || small_group) return rc;

@@ -70,15 +70,11 @@ constexpr int kTcPrepWarps = 8;
 constexpr int kTcXGroups = 2;  // x-term groups of four warps, alternating k-blocks
 constexpr int kTcEpiWarps = 4;
 constexpr int kTcXfrWarps = 4;  // weight transfer: one per TMEM sub-partition
-constexpr int kTcND = 4;   // accumulators in TMEM
+constexpr int kTcND = 4;   // accumulators in TMEM (two at 64 token slots)
 constexpr int kTcNB = 4;   // x-term tiles
 constexpr int kTcNX = 8;   // per-token scalars of a k-block
 constexpr int kTcNXR = 4;  // x k-blocks staged ahead of the x-term warps
-// Tensor memory: accumulators at columns d * 2 MP (d < kTcND); AWQ: tensor-
-// memory A tile t (t < kTcNA, 128 lanes x 128 bytes of widened weight) at
-// kTcTmemA + 32 t.
-constexpr int kTcNA = 4;
-constexpr uint32_t kTcTmemA = 256;
+constexpr int kTcNA = 4;  // AWQ tensor-memory A tiles
 
 constexpr int kTcMaxNS = 12;  // weight ring slots (upper bound; the plan sizes the ring to shared memory)
 constexpr int kTcSmemMax = 227 * 1024;
@@ -90,15 +86,35 @@ constexpr int kTcSmemMax = 227 * 1024;
 // PRE: the x terms come precomputed (tc_xterm_kernel, once per launch instead
 // of once per CTA): one warp copies them in by TMA in place of the eight
 // x-term warps.
-template <int FMT, bool PRE>
+// Epilogue: four warps (one per TMEM sub-partition), or with PRE and 32+
+// token slots eight, each taking half the token slots of its sub-partition.
+template <int FMT, int MP, bool PRE>
 struct TcCfg {
   static constexpr bool kTmemA = FMT == 0;
   static constexpr int kEpi0 = PRE ? kTcWarpPrep0 + 1 : kTcWarpPrep0 + kTcPrepWarps;  // first epilogue warp
-  static constexpr int kXfr0 = kEpi0 + kTcEpiWarps;                                   // first transfer warp
+  static constexpr int kEpiWarps = PRE && MP >= 32 ? 2 * kTcEpiWarps : kTcEpiWarps;
+  static constexpr int kXfr0 = kEpi0 + kEpiWarps;                                     // first transfer warp
   static constexpr int kXfrGroups = 1;  // transfer groups of four warps taking alternate ring slots (two: no faster)
   static constexpr int kThreads = (kTmemA ? kXfr0 + kXfrGroups * kTcXfrWarps : kXfr0) * 32;
   static constexpr int kKPS = FMT == 0 ? 2 : 1;  // k-blocks per ring slot
-  static constexpr uint32_t kTmemCols = kTmemA ? 512 : 256;
+};
+
+// Tensor memory and occupancy of one instantiation. Accumulators at columns
+// d * 2 MP (d < kND); AWQ: A tile t (t < kTcNA, 128 lanes x 128 bytes of
+// widened weight) at kA + 32 t. Two CTAs per SM (112 KB of shared memory and
+// at most 256 columns each, so that the next launch's CTA streams its weights
+// while this one finishes) measured slower than one CTA with the full ring:
+// FP8 4096 -> 14336 at M = 32 18.5 -> 22.7 us.
+template <int FMT, int MP, bool PRE>
+struct TcMem {
+  static constexpr bool kPair = false;  // two CTAs per SM measured slower (a smaller weight ring): one
+  static constexpr int kMinBlocks = kPair ? 2 : 1;
+  static constexpr int kSmem = kPair ? 112 * 1024 : kTcSmemMax;  // dynamic shared memory, alignment slack included
+  static constexpr int kND = MP == 64 ? 2 : kTcND;                // accumulators
+  static constexpr uint32_t kA = kND * 2 * MP;                    // AWQ A tiles after the accumulators
+  static constexpr uint32_t kUsed = kA + (FMT == 0 ? 32 * kTcNA : 0);
+  static constexpr uint32_t kCols = kUsed <= 128 ? 128 : kUsed <= 256 ? 256 : 512;
+  static_assert(!kPair || kCols <= 256, "two CTAs per SM share 512 columns");
 };
 
 // Fixed part of the shared-memory layout (after the weight ring, whose size
@@ -347,11 +363,12 @@ __device__ __forceinline__ void tc_x_terms(const uint4 (&v)[EPT / 8], uint32_t (
 }
 
 template <int FMT, bool BF16, int MP, bool PRE>
-__global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
+__global__ void __launch_bounds__(TcCfg<FMT, MP, PRE>::kThreads, (TcMem<FMT, MP, PRE>::kMinBlocks))
     decode_tc_kernel(const __grid_constant__ CUtensorMap wmap_lo, const __grid_constant__ CUtensorMap wmap_hi,
                      const __grid_constant__ CUtensorMap xmap, const TcParams p) {
   using F = TcFixed<MP, PRE>;
-  using C = TcCfg<FMT, PRE>;
+  using C = TcCfg<FMT, MP, PRE>;
+  using T = TcMem<FMT, MP, PRE>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* fx = smem + p.off_fixed;
@@ -407,18 +424,18 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
     }
     for (int i = 0; i < kTcND; ++i) {
       mbar_init(&dfull[i], 1);
-      mbar_init(&dempty[i], 4);
+      mbar_init(&dempty[i], C::kEpiWarps);
     }
     for (int i = 0; i < kTcNX; ++i) {
       mbar_init(&xsfull[i], 1);
-      mbar_init(&xsempty[i], 4);
+      mbar_init(&xsempty[i], C::kEpiWarps);
     }
     for (int i = 0; i < kTcNXR; ++i) mbar_init(&xfull[i], 1);
     mbar_init(mdone, 1);
     fence_barrier_init();
   }
   if (warp == kTcWarpMma) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_alloc(tmem_slot, T::kCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -452,20 +469,20 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
     // ---------------- UMMA issuer (whole warp, converged) ----------------
     const uint32_t idesc = tc_idesc(FMT, kTcM, 2 * MP);
     for (int b = 0; b < nkb; ++b) {
-      const int s = b % F::kNB, d = b % kTcND;  // x-term tile, accumulator
+      const int s = b % F::kNB, d = b % T::kND;  // x-term tile, accumulator
       // the A tile: FP8 ring slot b % ns; AWQ tensor-memory tile b % kTcNA
       const int a = FMT == 1 ? b % NS : b % kTcNA;
       uint64_t* abar = FMT == 1 ? &wfull[a] : &afull[a];
       const uint32_t apar = FMT == 1 ? ((b / NS) & 1) : ((b / kTcNA) & 1);
       const uint32_t bpar = (b / F::kNB) & 1;
-      const uint32_t dpar = ((b / kTcND) - 1) & 1;  // accumulator d free again (k-block b - kTcND read out)
+      const uint32_t dpar = ((b / T::kND) - 1) & 1;  // accumulator d free again (k-block b - T::kND read out)
       // the A tile, the x-term tile and the accumulator
       const bool ready = __all_sync(
-          0xffffffffu, mbar_test3(abar, apar, &bfull[s], bpar, b >= kTcND ? &dempty[d] : &bfull[s], b >= kTcND ? dpar : bpar));
+          0xffffffffu, mbar_test3(abar, apar, &bfull[s], bpar, b >= T::kND ? &dempty[d] : &bfull[s], b >= T::kND ? dpar : bpar));
       if (!ready) {
         ok = __all_sync(0xffffffffu, mbar_wait(abar, apar, p.status, FMT == 1 ? 81 : 82, abort_flag));
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bfull[s], bpar, p.status, 83, abort_flag));
-        if (ok && b >= kTcND) ok = __all_sync(0xffffffffu, mbar_wait(&dempty[d], dpar, p.status, 84, abort_flag));
+        if (ok && b >= T::kND) ok = __all_sync(0xffffffffu, mbar_wait(&dempty[d], dpar, p.status, 84, abort_flag));
         if (!ok) break;
       }
       tc_fence_after();
@@ -475,7 +492,7 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
         tc_umma_ss_f8(dt, sw128_kmajor_desc(smem_u32(smem) + (uint32_t)a * tile), bdesc, idesc);
         tc_commit3_elect(&wempty[a], &bempty[s], &dfull[d]);
       } else {
-        tc_umma_ts_i8(dt, tmem_base + kTcTmemA + 32u * (uint32_t)a, bdesc, idesc);
+        tc_umma_ts_i8(dt, tmem_base + T::kA + 32u * (uint32_t)a, bdesc, idesc);
         tc_commit3_elect(&aempty[a], &bempty[s], &dfull[d]);
       }
     }
@@ -508,6 +525,7 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
       }
     }
   } else if (warp < C::kEpi0) {
+    if constexpr (!PRE) {
     // ---------------- x terms ----------------
     pdl_wait_prior_grids();  // x is written by the previous kernel
     constexpr int kGT = kTcPrepWarps / kTcXGroups * 32;  // threads of a group
@@ -584,16 +602,19 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
         mbar_wait(&xfull[bb % kTcNXR], (bb / kTcNXR) & 1, nullptr, 0, nullptr);
       }
     }
+    }
   } else if (warp < C::kXfr0) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;  // TMEM sub-partition: rows 32 q .. 32 q + 31
+    constexpr int MPE = MP * kTcEpiWarps / C::kEpiWarps;  // token slots of this warp
+    const int t0 = (warp - C::kEpi0) / kTcEpiWarps * MPE;  // its first
     const int row = q * 32 + lane;
     const bool rv = row < rvalid;
     const int n = r0 + row;
     const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16);
-    float acc[MP];
+    float acc[MPE];
 #pragma unroll
-    for (int i = 0; i < MP; ++i) acc[i] = 0.f;
+    for (int i = 0; i < MPE; ++i) acc[i] = 0.f;
     const unsigned short* sc16 = reinterpret_cast<const unsigned short*>(p.scales);
     const unsigned short* zr16 = reinterpret_cast<const unsigned short*>(p.zeros);
     // AWQ: (scale, zero point) of this row for k-block b (0 past K or for rows past N)
@@ -605,24 +626,24 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
     // four k-blocks ahead (a global load's latency is about two k-blocks' time)
     uint32_t sz0 = load_sz(0), sz1 = load_sz(1), sz2 = load_sz(2), sz3 = load_sz(3);
     for (int b = 0; b < nkb; ++b) {
-      const int d = b % kTcND, xsl = b % kTcNX;
+      const int d = b % T::kND, xsl = b % kTcNX;
       const uint32_t sz = sz0;
       sz0 = sz1, sz1 = sz2, sz2 = sz3, sz3 = load_sz(b + 4);
       // the accumulator and the k-block's scalars
-      if (!mbar_test3(&dfull[d], (b / kTcND) & 1, &xsfull[xsl], (b / kTcNX) & 1, &xsfull[xsl], (b / kTcNX) & 1)) {
-        if (!(ok = mbar_wait(&dfull[d], (b / kTcND) & 1, p.status, 87, abort_flag))) break;
+      if (!mbar_test3(&dfull[d], (b / T::kND) & 1, &xsfull[xsl], (b / kTcNX) & 1, &xsfull[xsl], (b / kTcNX) & 1)) {
+        if (!(ok = mbar_wait(&dfull[d], (b / T::kND) & 1, p.status, 87, abort_flag))) break;
         if (!(ok = mbar_wait(&xsfull[xsl], (b / kTcNX) & 1, p.status, 88, abort_flag))) break;
       }
       tc_fence_after();
       const float s = __half2float(__ushort_as_half((unsigned short)(sz & 0xFFFFu)));
       const float z = __half2float(__ushort_as_half((unsigned short)(sz >> 16)));
-      const float* xsc = xs + (xsl * 2) * MP;
-      const float* xsx = xs + (xsl * 2 + 1) * MP;
+      const float* xsc = xs + (xsl * 2) * MP + t0;
+      const float* xsx = xs + (xsl * 2 + 1) * MP + t0;
 #pragma unroll
-      for (int th = 0; th < MP; th += 16) {
+      for (int th = 0; th < MPE; th += 16) {
         uint32_t ra[16], rb[16];
-        tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + th), ra);
-        tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + MP + th), rb);
+        tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + t0 + th), ra);
+        tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + MP + t0 + th), rb);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -647,10 +668,10 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
       const float bn = p.bias_dtype != NSQ_DTYPE_NONE ? load_bias(p.bias, p.bias_dtype, n) : 0.f;
       uint16_t* y = static_cast<uint16_t*>(p.y);
 #pragma unroll
-      for (int i = 0; i < MP; ++i) {
-        if (i < p.M) {
+      for (int i = 0; i < MPE; ++i) {
+        if (t0 + i < p.M) {
           const float v = acc[i] * ws + bn;
-          y[(int64_t)i * p.N + n] = float_to_elem<BF16>(v);
+          y[(int64_t)(t0 + i) * p.N + n] = float_to_elem<BF16>(v);
         }
       }
     }
@@ -713,7 +734,7 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
           o[4] = u.z & 0x0F0F0F0Fu, o[5] = (u.z >> 4) & 0x0F0F0F0Fu;
           o[6] = u.w & 0x0F0F0F0Fu, o[7] = (u.w >> 4) & 0x0F0F0F0Fu;
         }
-        const uint32_t ta = tl + kTcTmemA + 32u * (uint32_t)((b0 + h) % kTcNA);
+        const uint32_t ta = tl + T::kA + 32u * (uint32_t)((b0 + h) % kTcNA);
         tmem_st_32x32b_x16(ta, v0);
         tmem_st_32x32b_x16(ta + 16, v1);
       }
@@ -728,21 +749,21 @@ __global__ void __launch_bounds__(TcCfg<FMT, PRE>::kThreads, 1)
   __syncthreads();
   if (warp == kTcWarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    tmem_dealloc(tmem_base, T::kCols);
   }
 }
 
-// The x terms of one launch, once (one CTA per k-block, 128 threads, the
-// token's 128 / MP threads adjacent): the x-term tile of k-block b as rows
+// The x terms of one launch, once (one CTA per k-block, eight adjacent
+// threads per token slot, 16 columns each): the x-term tile of k-block b as rows
 // [b * 2 MP, b * 2 MP + 2 MP) of 128 bytes (T1 rows of the MP token slots,
 // then their T2 rows; unswizzled, the tensor map swizzles on the way in) and
 // its scalars xsg[b][0][tok] = 2^e, xsg[b][1][tok] = term sum (AWQ). Token
 // slots past M get zero terms.
 template <int FMT, bool BF16, int MP>
-__global__ void __launch_bounds__(128) tc_xterm_kernel(const void* x, int M, int K, uint8_t* xt, float* xsg) {
+__global__ void __launch_bounds__(MP * 8) tc_xterm_kernel(const void* x, int M, int K, uint8_t* xt, float* xsg) {
   pdl_launch_dependents();
   pdl_wait_prior_grids();  // x is written by the previous kernel
-  constexpr int TPT = 128 / MP, EPT = 128 / TPT;
+  constexpr int TPT = 8, EPT = 128 / TPT;
   const int b = (int)blockIdx.x, t = (int)threadIdx.x;
   const int tok = t / TPT, part = t - (t / TPT) * TPT;
   uint4 v[EPT / 8];
@@ -770,7 +791,7 @@ template <int FMT, bool BF16, int MP>
 cudaError_t launch_xterm(const void* x, int M, int K, uint8_t* xt, float* xsg, cudaStream_t stream) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(K / 128, 1, 1);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.blockDim = dim3(MP * 8, 1, 1);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   int na = 0;
@@ -790,13 +811,13 @@ cudaError_t launch_tc(const CUtensorMap& wlo, const CUtensorMap& whi, const CUte
   auto kern = decode_tc_kernel<FMT, BF16, MP, PRE>;
   static std::atomic<bool> configured{false};
   if (!configured.load()) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcMem<FMT, MP, PRE>::kSmem);
     if (e != cudaSuccess) return e;
     configured.store(true);
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(TcCfg<FMT, PRE>::kThreads, 1, 1);
+  cfg.blockDim = dim3(TcCfg<FMT, MP, PRE>::kThreads, 1, 1);
   cfg.dynamicSmemBytes = (size_t)p.off_fixed + TcFixed<MP, PRE>::kBytes + 1024;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -815,12 +836,16 @@ template <int FMT, bool BF16>
 cudaError_t dispatch_tc(int mp, bool pre, const CUtensorMap& wlo, const CUtensorMap& whi, const CUtensorMap& xmap,
                         const TcParams& p, int grid, const void* x, uint8_t* xt, cudaStream_t s) {
   if (pre) {
-    cudaError_t e = mp == 16 ? launch_xterm<FMT, BF16, 16>(x, p.M, p.K, xt, const_cast<float*>(p.xsg), s)
-                             : launch_xterm<FMT, BF16, 32>(x, p.M, p.K, xt, const_cast<float*>(p.xsg), s);
+    float* xsg = const_cast<float*>(p.xsg);
+    cudaError_t e = mp == 16   ? launch_xterm<FMT, BF16, 16>(x, p.M, p.K, xt, xsg, s)
+                    : mp == 32 ? launch_xterm<FMT, BF16, 32>(x, p.M, p.K, xt, xsg, s)
+                               : launch_xterm<FMT, BF16, 64>(x, p.M, p.K, xt, xsg, s);
     if (e != cudaSuccess) return e;
-    return mp == 16 ? launch_tc<FMT, BF16, 16, true>(wlo, whi, xmap, p, grid, s)
-                    : launch_tc<FMT, BF16, 32, true>(wlo, whi, xmap, p, grid, s);
+    return mp == 16   ? launch_tc<FMT, BF16, 16, true>(wlo, whi, xmap, p, grid, s)
+           : mp == 32 ? launch_tc<FMT, BF16, 32, true>(wlo, whi, xmap, p, grid, s)
+                      : launch_tc<FMT, BF16, 64, true>(wlo, whi, xmap, p, grid, s);
   }
+  if (mp == 64) return cudaErrorInvalidValue;  // 64 token slots only with precomputed terms
   return mp == 16 ? launch_tc<FMT, BF16, 16, false>(wlo, whi, xmap, p, grid, s)
                   : launch_tc<FMT, BF16, 32, false>(wlo, whi, xmap, p, grid, s);
 }
@@ -831,7 +856,7 @@ namespace {
 // Rows per CTA in multiples of 8 (so every k-block tile of a stage stays on a
 // 1 KB swizzle boundary): rlo for most CTAs, rlo + 8 for the first nhi.
 bool tc_rows(const LinearArgs& a, int* rlo, int* nhi, int* grid) {
-  if (a.M < 1 || a.M > 32 || a.K % 128 != 0 || a.K < 256) return false;
+  if (a.M < 1 || a.M > 64 || a.K % 128 != 0 || a.K < 256) return false;
   if (a.fmt == 0 && (a.K % 256 != 0 || a.group_size % 128 != 0 || a.K % a.group_size != 0)) return false;
   const int sms = num_sms();
   const int g8 = (a.N + 7) / 8;
@@ -851,8 +876,11 @@ int decode_tc_rows(const LinearArgs& a) {
   return rlo + (nhi > 0 ? 8 : 0);
 }
 
+// token slots of a launch: 16, 32 or 64 (64 only with precomputed x terms)
+static int tc_slots(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : 64; }
+
 size_t decode_tc_workspace_bytes(const LinearArgs& a) {
-  const int64_t nkb = a.K / 128, rows = nkb * 2 * (a.M <= 16 ? 16 : 32);
+  const int64_t nkb = a.K / 128, rows = nkb * 2 * tc_slots(a.M);
   return (size_t)(rows * 128 + rows * 4);
 }
 
@@ -860,11 +888,12 @@ int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
   int rlo, nhi, grid;
   if (!tc_rows(a, &rlo, &nhi, &grid)) return NSQ_ENOTSUP;
   const int rmax = rlo + (nhi > 0 ? 8 : 0);
-  const int mp = a.M <= 16 ? 16 : 32;
+  const int mp = tc_slots(a.M);
   // with a workspace, the x terms are computed once by tc_xterm_kernel: the
   // terms [nkb x 2 mp rows][128 B], then the scalars [nkb][2][mp] fp32
   const bool pre = a.ws != nullptr && a.ws_bytes >= decode_tc_workspace_bytes(a) && ((uintptr_t)a.ws & 15) == 0;
   uint8_t* xt = static_cast<uint8_t*>(a.ws);
+  if (mp == 64 && !pre) return NSQ_ENOTSUP;
   TcParams p{};
   p.x = a.x;
   p.scales = reinterpret_cast<const __half*>(a.scales);
@@ -885,7 +914,8 @@ int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
   // Shared memory: the weight ring (sized to what is left, at most kTcMaxNS
   // slots of the tallest CTA's rows x 128 B), then the fixed part.
   p.tile = rmax * 128;
-  const int fixed = pre ? (mp == 16 ? TcFixed<16, true>::kBytes : TcFixed<32, true>::kBytes)
+  const int fixed = pre ? (mp == 16 ? TcFixed<16, true>::kBytes : mp == 32 ? TcFixed<32, true>::kBytes
+                                                                        : TcFixed<64, true>::kBytes)
                         : (mp == 16 ? TcFixed<16, false>::kBytes : TcFixed<32, false>::kBytes);
   const int room = kTcSmemMax - 1024 - fixed;
   p.ns = room / p.tile;

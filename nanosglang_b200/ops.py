@@ -93,7 +93,7 @@ def _decode_workspace(lib, quant: int, m: int, k: int, n: int, group_size: int, 
     else (None, 0). The tensor comes from the caching allocator on the
     current stream, so its reuse is stream-ordered after the launches that
     read it (also under CUDA-graph capture)."""
-    if m > 32:
+    if m > 64:
         return None, 0
     nbytes = lib.nsq_linear_workspace_size(quant, m, k, n, group_size)
     if not nbytes:

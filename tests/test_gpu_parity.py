@@ -201,7 +201,9 @@ def test_awq_linear_decode_large_layer(m):
     (32, 14336, 4096, 256, "frac", torch.bfloat16, False),  # groups of two k-blocks, fractional zero points
     (28, 12288, 2048, 128, "int", torch.float16, True),
     (16, 18944, 4096, 128, "int", torch.bfloat16, False),   # 128 rows per CTA; 56 M+ weight elements at M = 16
-    (5, 18944, 8192, 128, "frac", torch.bfloat16, False)])  # few tokens on a weight with no weight-ring plan
+    (5, 18944, 8192, 128, "frac", torch.bfloat16, False),   # few tokens on a weight with no weight-ring plan
+    (48, 14336, 4096, 128, "frac", torch.bfloat16, True),   # 64 token slots (precomputed x terms)
+    (64, 10000, 2048, 128, "int", torch.float16, False)])
 def test_awq_linear_tensor_core_decode(m, n, k, gs, zm, dtype, bias):
     """Layers of 64-128 rows per SM at M <= 32, shapes the dispatch sends to the tcgen05 decode kernel (nibbles
     widened to u8 in tensor memory, x as two s8 terms per k-block, kind::i8 UMMAs, zero point and scale per k-block
@@ -340,7 +342,9 @@ def test_fp8_linear_decode_large_layer(m):
     (2, 9472, 2048, torch.bfloat16, False),   # 64 rows per CTA
     (13, 10000, 896, torch.bfloat16, True),   # 64 / 72 rows per CTA, K of seven k-blocks
     (16, 14336, 4096, torch.float16, True),
-    (32, 18944, 2048, torch.bfloat16, False)])  # 128 rows per CTA
+    (32, 18944, 2048, torch.bfloat16, False),  # 128 rows per CTA
+    (64, 14336, 4096, torch.bfloat16, True),   # 64 token slots (precomputed x terms)
+    (40, 18944, 3584, torch.float16, False)])
 def test_fp8_linear_tensor_core_decode(m, n, k, dtype, bias):
     """Layers of 64-128 rows per SM, shapes the dispatch sends to the tcgen05 decode kernel (kind::f8f6f4 UMMAs on
     the stored e4m3 codes, x as two e4m3 terms per token and k-block)."""
