@@ -282,16 +282,18 @@ int nsq_fp8_dequant(const uint8_t* weight_fp8, const float* weight_scale, void* 
 //   40.9 vs 47.3 (the one-CTA prefill kernel), 8192 -> 18944 76.4 vs 92.3;
 //   FP8 4096 -> 14336 24.6 vs 25.8, 8192 -> 18944 40.5 vs 47.0; FP8 below
 //   32 M weight elements (2048 -> 10000) is a tie and stays.
-static bool tc_decode_chosen(const LinearArgs& a) {
+// pre: the call has the workspace for precomputed x terms (AWQ at 9..32
+// tokens then wins from K >= 2048 on: 4096 -> 12288 at M = 16 19.4 vs 21.7).
+static bool tc_decode_chosen(const LinearArgs& a, bool pre) {
   if (a.M > 64 || (a.fmt == 0 && a.group_size % 128 != 0)) return false;
   const int64_t kn = (int64_t)a.K * a.N;
   // 33..64 tokens run only with precomputed x terms (a workspace)
   const bool tc_wins =
-      a.M > 32 ? a.K >= 2048 && (a.fmt == 0 || kn >= ((int64_t)1 << 25))
+      a.M > 32     ? pre && a.K >= 2048 && (a.fmt == 0 || kn >= ((int64_t)1 << 25))
       : a.fmt == 1 ? (a.K >= 2048 || (a.M > 8 && a.M <= 16) || a.M > 24)
-                 : a.K >= 2048 && (a.M > 24 || (a.M > 16   ? kn >= ((int64_t)1 << 26)
-                                                : a.M > 8 ? kn >= ((int64_t)7 << 23)
-                                                          : kn >= ((int64_t)1 << 27)));
+      : a.K < 2048 ? false
+      : a.M > 8    ? (pre || a.M > 24 || kn >= (a.M > 16 ? ((int64_t)1 << 26) : ((int64_t)7 << 23)))
+                   : kn >= ((int64_t)1 << 27);
   return tc_wins && decode_tc_rows(a) > 0;
 }
 
@@ -311,7 +313,7 @@ static int linear_common(LinearArgs& a, cudaStream_t stream) {
     // work grows with the token count (B200, CUDA-graph chains, AWQ at
     // M = 64: Llama-3-8B gate 140 -> 47 us, down 146 -> 47 us, q 52 -> 18 us,
     // 896 -> 9728 19.5 -> 12.6 us; 4096 -> 1024 stays faster on mma.sync)
-    if (tc_decode_chosen(a)) {
+    if (tc_decode_chosen(a, a.ws_bytes >= decode_tc_workspace_bytes(a) && ((uintptr_t)a.ws & 15) == 0)) {
       const int rc = run_decode_tc_linear(a, stream);
       if (rc != NSQ_ENOTSUP) return rc;
     }
@@ -373,7 +375,7 @@ size_t nsq_linear_workspace_size(int quant, int64_t M, int64_t K, int64_t N, int
   a.N = (int)N;
   a.group_size = quant == 0 ? (int)group_size : 0;
   if (quant == 0 && (group_size <= 0 || group_size > kIntMax)) return 0;
-  return tc_decode_chosen(a) ? decode_tc_workspace_bytes(a) : 0;
+  return tc_decode_chosen(a, true) ? decode_tc_workspace_bytes(a) : 0;
 }
 
 int nsq_awq_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
