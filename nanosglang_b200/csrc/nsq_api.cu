@@ -294,6 +294,12 @@ static bool tc_decode_chosen(const LinearArgs& a, bool pre) {
       : a.K < 2048 ? false
       : a.M > 8    ? (pre || a.M > 24 || kn >= (a.M > 16 ? ((int64_t)1 << 26) : ((int64_t)7 << 23)))
                    : kn >= ((int64_t)1 << 27);
+  // Layers of fewer than 64 rows per SM run on fewer CTAs of 64+ rows: a win
+  // for K <= 4096 at up to 32 tokens (TP shards: AWQ 4096 -> 7168 at M = 16
+  // 23.4 -> 18.3 us, FP8 at M = 32 20.9 -> 17.4 us), a loss at 64 tokens or
+  // K = 8192 (FP8 8192 -> 7392 at M = 64 28.1 -> 38.6 us), and below 96 CTAs.
+  const bool full_grid = (int64_t)a.N >= (int64_t)64 * num_sms();
+  if (!full_grid && (a.N < 6144 || a.K > 4096 || a.M > 32)) return false;
   return tc_wins && decode_tc_rows(a) > 0;
 }
 

@@ -30,7 +30,8 @@
 //
 // Work split: CTA i owns a block of weight rows, a multiple of 8 between 64 and
 // 128 (TMEM lane = row; one TMA box of [rows x 128 B] per ring slot), and the
-// whole K range: accumulators never leave the CTA, no split-K, no workspace.
+// whole K range: accumulators never leave the CTA, no split-K. One CTA per SM,
+// or fewer CTAs of 64+ rows on smaller layers.
 // Warp roles (FP8 448 threads, AWQ 576):
 //   warp 0      TMA producer (one lane): one 128-byte chunk of every row per
 //               ring slot -- an FP8 k-block, which is the UMMA A tile itself,
@@ -860,7 +861,8 @@ bool tc_rows(const LinearArgs& a, int* rlo, int* nhi, int* grid) {
   if (a.fmt == 0 && (a.K % 256 != 0 || a.group_size % 128 != 0 || a.K % a.group_size != 0)) return false;
   const int sms = num_sms();
   const int g8 = (a.N + 7) / 8;
-  const int c = g8 < sms ? g8 : sms;
+  // one CTA per SM, or fewer on smaller layers so that a CTA keeps >= 64 rows
+  const int c = g8 / 8 < sms ? (g8 / 8 > 0 ? g8 / 8 : 1) : sms;
   const int base = g8 / c, rem = g8 - base * c;
   *rlo = 8 * base;
   *nhi = rem;

@@ -90,8 +90,9 @@ struct RowsLaunch {
 };
 int run_decode_rows(const RowsLaunch& L, cudaStream_t stream);
 int run_decode_rows_linear(const LinearArgs& a, cudaStream_t stream);
-// Tensor-core decode kernel (M <= 32, K % 128 == 0, AWQ groups of 128 k, 64 to
-// 128 weight rows per SM): rows per CTA, or 0 if it does not apply.
+// Tensor-core decode kernel (M <= 64, K % 128 == 0, AWQ groups of 128 k, 64 to
+// 128 weight rows per CTA; one CTA per SM, fewer on layers of fewer than 64
+// rows per SM): rows of the tallest CTA, or 0 if it does not apply.
 int decode_tc_rows(const LinearArgs& a);
 // Workspace with which the kernel takes precomputed x terms (one small kernel
 // ahead of it instead of every CTA computing them); without it, the CTAs do.

@@ -203,6 +203,7 @@ def test_awq_linear_decode_large_layer(m):
     (16, 18944, 4096, 128, "int", torch.bfloat16, False),   # 128 rows per CTA; 56 M+ weight elements at M = 16
     (5, 18944, 8192, 128, "frac", torch.bfloat16, False),   # few tokens on a weight with no weight-ring plan
     (48, 14336, 4096, 128, "frac", torch.bfloat16, True),   # 64 token slots (precomputed x terms)
+    (16, 7168, 4096, 128, "int", torch.bfloat16, True),     # fewer than 64 rows per SM: 112 CTAs of 64 rows
     (64, 10000, 2048, 128, "int", torch.float16, False)])
 def test_awq_linear_tensor_core_decode(m, n, k, gs, zm, dtype, bias):
     """Layers of 64-128 rows per SM at M <= 32, shapes the dispatch sends to the tcgen05 decode kernel (nibbles
@@ -344,6 +345,7 @@ def test_fp8_linear_decode_large_layer(m):
     (16, 14336, 4096, torch.float16, True),
     (32, 18944, 2048, torch.bfloat16, False),  # 128 rows per CTA
     (64, 14336, 4096, torch.bfloat16, True),   # 64 token slots (precomputed x terms)
+    (32, 6600, 4096, torch.float16, True),     # fewer than 64 rows per SM: 103 CTAs, some of 72 rows
     (40, 18944, 3584, torch.float16, False)])
 def test_fp8_linear_tensor_core_decode(m, n, k, dtype, bias):
     """Layers of 64-128 rows per SM, shapes the dispatch sends to the tcgen05 decode kernel (kind::f8f6f4 UMMAs on
