@@ -153,6 +153,7 @@ struct TcParams {
   int tile;       // bytes of a ring slot: the tallest CTA's rows x 128 B
   int ns;         // weight ring slots (at shared-memory offset 0)
   int off_fixed;  // the fixed part (TcFixed)
+  int sz_vec;     // AWQ: G % 8 == 0 and 16-byte aligned scales / zeros (eight groups per load)
   const float* xsg;  // PRE: per-k-block scalars [nkb][2][MP] (the terms: tensor map bmap)
 };
 
@@ -287,7 +288,8 @@ __device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t codes16) {
 // The x terms of one token's EPT columns of a k-block (this thread's share;
 // the token's TPT threads are adjacent lanes and reduce the block's largest
 // |x| and the term sums by shuffles): term bytes o1 (T1) and o2 (T2) in the A
-// operand's column order, the scale sc = 2^e and (AWQ) the term sum sx.
+// operand's column order, the scale sc = 2^e and (AWQ) sx = 2^e times the
+// term sum (the zero point's factor in the epilogue).
 template <int FMT, bool BF16, int EPT, int TPT>
 __device__ __forceinline__ void tc_x_terms(const uint4 (&v)[EPT / 8], uint32_t (&o1)[EPT / 4], uint32_t (&o2)[EPT / 4],
                                            float& sc, float& sx) {
@@ -361,6 +363,7 @@ __device__ __forceinline__ void tc_x_terms(const uint4 (&v)[EPT / 8], uint32_t (
   // an infinite or NaN x makes the token's outputs NaN, as the reference's
   // matmul would (the terms of such a block are meaningless)
   if (E == 255) sc = __int_as_float(0x7FC00000);
+  if constexpr (FMT == 0) sx *= sc;
 }
 
 template <int FMT, bool BF16, int MP, bool PRE>
@@ -624,12 +627,39 @@ __global__ void __launch_bounds__(TcCfg<FMT, MP, PRE>::kThreads, (TcMem<FMT, MP,
       const int64_t off = (int64_t)n * p.G + (b * 128) / p.group_size;
       return (uint32_t)__ldg(sc16 + off) | ((uint32_t)__ldg(zr16 + off) << 16);
     };
+    // Either eight groups' scales and zero points per 16-byte load (p.sz_vec:
+    // G % 8 == 0, 16-byte aligned rows), the next eight loaded when the
+    // current eight start; or one (scale, zero) per k-block, four ahead.
+    const bool vec = FMT == 0 && p.sz_vec && rv;
+    const int kpg = FMT == 0 ? p.group_size / 128 : 1;  // k-blocks per group
+    const uint4* srow = reinterpret_cast<const uint4*>(sc16 + (int64_t)n * p.G);
+    const uint4* zrow = reinterpret_cast<const uint4*>(zr16 + (int64_t)n * p.G);
+    const uint4 kZero4 = make_uint4(0u, 0u, 0u, 0u);
+    uint4 s_cur = kZero4, z_cur = kZero4, s_nxt = kZero4, z_nxt = kZero4;
+    int cur_c = 0;
+    if (vec) {
+      s_cur = __ldg(srow), z_cur = __ldg(zrow);
+      if (p.G > 8) s_nxt = __ldg(srow + 1), z_nxt = __ldg(zrow + 1);
+    }
     // four k-blocks ahead (a global load's latency is about two k-blocks' time)
-    uint32_t sz0 = load_sz(0), sz1 = load_sz(1), sz2 = load_sz(2), sz3 = load_sz(3);
+    uint32_t sz0 = 0u, sz1 = 0u, sz2 = 0u, sz3 = 0u;
+    if (!vec) sz0 = load_sz(0), sz1 = load_sz(1), sz2 = load_sz(2), sz3 = load_sz(3);
     for (int b = 0; b < nkb; ++b) {
       const int d = b % T::kND, xsl = b % kTcNX;
-      const uint32_t sz = sz0;
-      sz0 = sz1, sz1 = sz2, sz2 = sz3, sz3 = load_sz(b + 4);
+      uint32_t sz;
+      if (vec) {
+        const int gi = b / kpg, c = gi >> 3, j = gi & 7;
+        if (c != cur_c) {
+          s_cur = s_nxt, z_cur = z_nxt, cur_c = c;
+          if (8 * (c + 1) < p.G) s_nxt = __ldg(srow + c + 1), z_nxt = __ldg(zrow + c + 1);
+        }
+        const uint32_t sw = j < 4 ? (j < 2 ? s_cur.x : s_cur.y) : (j < 6 ? s_cur.z : s_cur.w);
+        const uint32_t zw = j < 4 ? (j < 2 ? z_cur.x : z_cur.y) : (j < 6 ? z_cur.z : z_cur.w);
+        sz = (j & 1) ? ((sw >> 16) | (zw & 0xFFFF0000u)) : ((sw & 0xFFFFu) | (zw << 16));
+      } else {
+        sz = sz0;
+        sz0 = sz1, sz1 = sz2, sz2 = sz3, sz3 = load_sz(b + 4);
+      }
       // the accumulator and the k-block's scalars
       if (!mbar_test3(&dfull[d], (b / T::kND) & 1, &xsfull[xsl], (b / kTcNX) & 1, &xsfull[xsl], (b / kTcNX) & 1)) {
         if (!(ok = mbar_wait(&dfull[d], (b / T::kND) & 1, p.status, 87, abort_flag))) break;
@@ -638,20 +668,33 @@ __global__ void __launch_bounds__(TcCfg<FMT, MP, PRE>::kThreads, (TcMem<FMT, MP,
       tc_fence_after();
       const float s = __half2float(__ushort_as_half((unsigned short)(sz & 0xFFFFu)));
       const float z = __half2float(__ushort_as_half((unsigned short)(sz >> 16)));
-      const float* xsc = xs + (xsl * 2) * MP + t0;
-      const float* xsx = xs + (xsl * 2 + 1) * MP + t0;
+      // AWQ: y += s 2^e (D1 + D2 / 128) - s z 2^e (S1 + S2 / 128), with 2^e and
+      // 2^e (S1 + S2 / 128) the k-block's two scalars of the token
+      const float u = s * 0.0078125f, w = -s * z;
+      const float4* xsc4 = reinterpret_cast<const float4*>(xs + (xsl * 2) * MP + t0);
+      const float4* xsx4 = reinterpret_cast<const float4*>(xs + (xsl * 2 + 1) * MP + t0);
 #pragma unroll
       for (int th = 0; th < MPE; th += 16) {
         uint32_t ra[16], rb[16];
         tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + t0 + th), ra);
         tmem_ld_32x32b_x16(tq + (uint32_t)(d * 2 * MP + MP + t0 + th), rb);
+        float sc4[16], sx4[16];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 cv = xsc4[th / 4 + q4];
+          sc4[4 * q4] = cv.x, sc4[4 * q4 + 1] = cv.y, sc4[4 * q4 + 2] = cv.z, sc4[4 * q4 + 3] = cv.w;
+          if constexpr (FMT == 0) {
+            const float4 xv = xsx4[th / 4 + q4];
+            sx4[4 * q4] = xv.x, sx4[4 * q4 + 1] = xv.y, sx4[4 * q4 + 2] = xv.z, sx4[4 * q4 + 3] = xv.w;
+          }
+        }
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float scl = xsc[th + i];
+          const float scl = sc4[i];
           if constexpr (FMT == 0) {
             const float v = (float)((int)ra[i] * 128 + (int)rb[i]);
-            acc[th + i] = fmaf(s * scl, fmaf(v, 0.0078125f, -z * xsx[th + i]), acc[th + i]);
+            acc[th + i] = fmaf(scl, u * v, fmaf(w, sx4[i], acc[th + i]));
           } else {
             acc[th + i] = fmaf(__uint_as_float(ra[i]), scl, fmaf(__uint_as_float(rb[i]), scl * 0.0625f, acc[th + i]));
           }
@@ -909,6 +952,7 @@ int run_decode_tc_linear(const LinearArgs& a, cudaStream_t stream) {
   p.N = a.N;
   p.group_size = a.fmt == 0 ? a.group_size : 0;
   p.G = a.fmt == 0 ? a.K / a.group_size : 0;
+  p.sz_vec = a.fmt == 0 && p.G % 8 == 0 && ((uintptr_t)a.scales & 15) == 0 && ((uintptr_t)a.zeros & 15) == 0;
   p.bias_dtype = a.bias ? a.bias_dtype : NSQ_DTYPE_NONE;
   p.rlo = rlo;
   p.nhi = nhi;
