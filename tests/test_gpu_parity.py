@@ -204,6 +204,7 @@ def test_awq_linear_decode_large_layer(m):
     (5, 18944, 8192, 128, "frac", torch.bfloat16, False),   # few tokens on a weight with no weight-ring plan
     (48, 14336, 4096, 128, "frac", torch.bfloat16, True),   # 64 token slots (precomputed x terms)
     (16, 7168, 4096, 128, "int", torch.bfloat16, True),     # fewer than 64 rows per SM: 112 CTAs of 64 rows
+    (12, 18944, 3584, 128, "frac", torch.bfloat16, False),  # 28 groups per row: scales loaded one group at a time
     (64, 10000, 2048, 128, "int", torch.float16, False)])
 def test_awq_linear_tensor_core_decode(m, n, k, gs, zm, dtype, bias):
     """Layers of 64-128 rows per SM at M <= 32, shapes the dispatch sends to the tcgen05 decode kernel (nibbles
